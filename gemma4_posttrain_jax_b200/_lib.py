@@ -1,0 +1,106 @@
+"""ctypes binding of liblp_b200.so (the C ABI declared in include/lp_logprob.h).
+
+The shared library is built in-tree (``python -m gemma4_posttrain_jax_b200.build``).
+There is no fallback: if the library is missing or fails to load, every call raises
+``LogprobLibraryError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "liblp_b200.so"
+
+LP_OK = 0
+LP_EINVAL = -1
+LP_ECUDA = -2
+LP_EWORKSPACE = -3
+LP_EDEVICE = -4
+LP_EUNSUPPORTED = -5
+
+LP_BWD_DH_F32 = 1
+LP_BWD_DW_BF16 = 2
+LP_BWD_NO_DW = 4
+LP_BWD_NO_DH = 8
+
+# Every symbol include/lp_logprob.h declares, with its ctypes signature.
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_SIG = {
+    "lp_version": (ctypes.c_int, []),
+    "lp_last_error": (ctypes.c_char_p, []),
+    "lp_launch_count": (ctypes.c_longlong, []),
+    "lp_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "lp_fwd_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
+    "lp_fwd": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, ctypes.c_float, _P, _P, _P, ctypes.c_size_t]),
+    "lp_combine": (ctypes.c_int, [_P, _P, ctypes.c_int, _I64, _P, _P]),
+    "lp_bwd_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, ctypes.c_int]),
+    "lp_bwd": (
+        ctypes.c_int,
+        [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, ctypes.c_float, _P, _P, _P, _I64, _P, ctypes.c_int, _I64, _P,
+         ctypes.c_size_t],
+    ),
+    "lp_compact_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
+    "lp_compact": (
+        ctypes.c_int,
+        [_P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t],
+    ),
+    "lp_gemm_bf16": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, ctypes.c_int, _P, _I64, _I64, ctypes.c_int, _P, _I64]),
+    "lp_scatter_rows": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _I64, ctypes.c_int, _P, _I64, _I64, _I64]),
+}
+EXPORTED_SYMBOLS = tuple(_SIG)
+
+
+class LogprobLibraryError(RuntimeError):
+    """The CUDA library is missing, failed to load, or returned an error code."""
+
+
+_lib: ctypes.CDLL | None = None
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load (once) and return the library with every declared symbol typed."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise LogprobLibraryError(
+            f"{p} is missing; build it with `python -m gemma4_posttrain_jax_b200.build` (nvcc, sm_100a). "
+            "The cuda logprob backend has no CPU fallback."
+        )
+    try:
+        lib = ctypes.CDLL(str(p))
+    except OSError as exc:  # pragma: no cover - depends on the host
+        raise LogprobLibraryError(f"cannot load {p}: {exc}") from exc
+    for name, (res, args) in _SIG.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def check(rc: int, what: str) -> None:
+    """Raise ``ValueError`` for argument errors and ``LogprobLibraryError`` otherwise."""
+    if rc == LP_OK:
+        return
+    msg = (load().lp_last_error() or b"").decode(errors="replace")
+    if rc == LP_EINVAL:
+        raise ValueError(f"{what}: {msg}")
+    raise LogprobLibraryError(f"{what} failed ({rc}): {msg}")
+
+
+def device_error(device: int) -> int:
+    """Read and clear the device-side error code of the library on ``device`` (syncs it)."""
+    code = ctypes.c_int(0)
+    check(load().lp_device_error(device, ctypes.byref(code)), "lp_device_error")
+    return code.value
+
+
+def launch_count() -> int:
+    """Kernels launched by the library in this process so far."""
+    return int(load().lp_launch_count())

@@ -1,0 +1,569 @@
+// C ABI of liblp_b200.so (declared in include/lp_logprob.h): argument checks, tensor-map
+// construction, tile planning and kernel launches. No torch or Python types cross it.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/lp_logprob.h"
+#include "lp_gemm.cuh"
+#include "lp_small_kernels.cuh"
+
+namespace {
+
+using namespace lpk;
+
+thread_local std::string g_last_error;
+std::atomic<long long> g_launches{0};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define LP_CUDA_TRY(expr)                                                                   \
+  do {                                                                                      \
+    cudaError_t e_ = (expr);                                                                \
+    if (e_ != cudaSuccess) return fail(LP_ECUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+#define LP_LAUNCH_CHECK(name)                                                                  \
+  do {                                                                                         \
+    cudaError_t e_ = cudaGetLastError();                                                       \
+    if (e_ != cudaSuccess) return fail(LP_ECUDA, "launch %s: %s", name, cudaGetErrorString(e_)); \
+    g_launches.fetch_add(1, std::memory_order_relaxed);                                        \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0, minor = 0;
+  bool ready = false;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int current_device_info(DeviceInfo** out) {
+  int dev = 0;
+  LP_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(LP_EINVAL, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    LP_CUDA_TRY(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    LP_CUDA_TRY(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev));
+    LP_CUDA_TRY(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev));
+    d.ready = true;
+  }
+  if (d.major != 10 || d.minor != 0)
+    return fail(LP_EUNSUPPORTED, "liblp_b200 needs an sm_100 (B200) device, device %d is sm_%d%d", dev, d.major,
+                d.minor);
+  *out = &d;
+  return LP_OK;
+}
+
+// --------------------------------------------------------------------------- tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D tiled map, 128-byte swizzle, zero fill out of bounds. `inner`/`outer` in elements,
+// `row_bytes` = byte stride between outer rows.
+int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize, uint64_t inner, uint64_t outer,
+             uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, const char* what) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(LP_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  if (inner == 0 || outer == 0) return fail(LP_EINVAL, "%s: empty tensor", what);
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return fail(LP_EINVAL, "%s: base pointer not 16-byte aligned", what);
+  if (row_bytes % 16 != 0) return fail(LP_EINVAL, "%s: row stride %llu bytes not a multiple of 16", what,
+                                       (unsigned long long)row_bytes);
+  if (row_bytes < inner * (uint64_t)esize) return fail(LP_EINVAL, "%s: row stride smaller than a row", what);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LP_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+  return LP_OK;
+}
+
+int map_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems, uint32_t bi,
+             uint32_t bo, const char* what) {
+  return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, outer, ld_elems * 2, bi, bo, what);
+}
+int map_f32(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems, uint32_t bi,
+            uint32_t bo, const char* what) {
+  return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, inner, outer, ld_elems * 4, bi, bo, what);
+}
+
+// --------------------------------------------------------------------------- planning
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Forward: N tiles grouped G per unit; pick the largest G within 1% of the best critical
+// path (units are dealt round-robin to `sms` persistent CTAs).
+GemmSched plan_fwd(int64_t T, int64_t Vs, int64_t d, int sms) {
+  GemmSched s{};
+  s.M = (int)T;
+  s.N = (int)Vs;
+  s.K = (int)d;
+  s.tiles_m = (int)cdiv(T, BM);
+  s.tiles_n = (int)cdiv(Vs, BN);
+  s.k_blocks = (int)cdiv(d, BK);
+  s.k_splits = 1;
+  s.kb_per_split = s.k_blocks;
+  s.n_fast = 0;
+  double best = 1e300;
+  int gmax = std::min(s.tiles_n, 256);
+  double cost[257];
+  for (int g = 1; g <= gmax; ++g) {
+    const int64_t units = (int64_t)s.tiles_m * cdiv(s.tiles_n, g);
+    cost[g] = (double)cdiv(units, sms) * g + 0.05 * g / std::max(1, s.tiles_n);
+    best = std::min(best, cost[g]);
+  }
+  int pick = 1;
+  for (int g = 1; g <= gmax; ++g)
+    if (cost[g] <= best * 1.01) pick = g;
+  s.n_group = pick;
+  s.n_groups = (int)cdiv(s.tiles_n, pick);
+  s.num_units = s.tiles_m * s.n_groups;
+  return s;
+}
+
+// Plain GEMM with optional split-K: pick S in [1, 16] minimising the critical path,
+// keeping at least 8 K blocks per split; ties prefer fewer splits.
+GemmSched plan_gemm(int64_t M, int64_t N, int64_t K, int sms, bool allow_split, int n_fast) {
+  GemmSched s{};
+  s.M = (int)M;
+  s.N = (int)N;
+  s.K = (int)K;
+  s.tiles_m = (int)cdiv(M, BM);
+  s.tiles_n = (int)cdiv(N, BN);
+  s.k_blocks = (int)cdiv(K, BK);
+  s.n_group = 1;
+  s.n_groups = s.tiles_n;
+  s.n_fast = n_fast;
+  const int64_t tiles = (int64_t)s.tiles_m * s.tiles_n;
+  int best_s = 1;
+  double best = 1e300;
+  const int smax = allow_split ? 16 : 1;
+  for (int sp = 1; sp <= smax; ++sp) {
+    const int64_t kb = cdiv(s.k_blocks, sp);
+    if (sp > 1 && kb < 8) break;
+    const int64_t real_splits = cdiv(s.k_blocks, kb);
+    if (real_splits != sp) continue;
+    const double c = (double)cdiv(tiles * sp, sms) * kb * (1.0 + 0.02 * (sp > 1));
+    if (c < best * 0.995) {
+      best = c;
+      best_s = sp;
+    }
+  }
+  s.kb_per_split = (int)cdiv(s.k_blocks, best_s);
+  s.k_splits = (int)cdiv(s.k_blocks, s.kb_per_split);
+  s.num_units = (int)(tiles * s.k_splits);
+  return s;
+}
+
+int64_t default_token_chunk(int64_t T, int64_t Vs) {
+  const int64_t ldz = (Vs + 7) / 8 * 8;
+  const int64_t budget = int64_t(4) << 30;  // bytes of bf16 dZ per chunk
+  int64_t tc = budget / (ldz * 2);
+  tc = std::max<int64_t>(BM, tc / BM * BM);
+  return std::min<int64_t>(tc, std::max<int64_t>(T, 1));
+}
+
+struct BwdLayout {
+  int64_t tc, chunks, ldz;
+  size_t dz_off, part_off, dwacc_off, total;
+  int max_splits;
+  int64_t mpad;
+};
+
+BwdLayout bwd_layout(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int flags, int sms) {
+  BwdLayout L{};
+  L.tc = token_chunk > 0 ? std::min<int64_t>(token_chunk, std::max<int64_t>(T, 1)) : default_token_chunk(T, Vs);
+  L.chunks = T > 0 ? cdiv(T, L.tc) : 0;
+  L.ldz = (Vs + 7) / 8 * 8;
+  L.mpad = cdiv(L.tc, BM) * BM;
+  // the largest split-K of any chunk (the first chunk is the largest)
+  L.max_splits = 1;
+  if (!(flags & LP_BWD_NO_DH) && T > 0) {
+    GemmSched s = plan_gemm(L.tc, d, Vs, sms, true, 1);
+    L.max_splits = s.k_splits;
+    // a shorter last chunk may choose more splits
+    const int64_t last = T - (L.chunks - 1) * L.tc;
+    GemmSched s2 = plan_gemm(last, d, Vs, sms, true, 1);
+    L.max_splits = std::max(L.max_splits, s2.k_splits);
+  }
+  size_t off = 0;
+  L.dz_off = off;
+  off += align_up((size_t)L.tc * L.ldz * 2, 1024);
+  L.part_off = off;
+  if (L.max_splits > 1) off += align_up((size_t)L.max_splits * L.mpad * d * 4, 1024);
+  L.dwacc_off = off;
+  if (!(flags & LP_BWD_NO_DW) && (flags & LP_BWD_DW_BF16) && L.chunks > 1) off += align_up((size_t)Vs * d * 4, 1024);
+  L.total = off;
+  return L;
+}
+
+// --------------------------------------------------------------------------- launches
+template <int EPI, bool A_MN, bool B_MN, bool CAP>
+int launch_gemm(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
+                const GemmParams& p, int sms) {
+  auto kern = tc_gemm_kernel<EPI, A_MN, B_MN, CAP>;
+  constexpr int smem = gemm_smem_bytes<EPI>();
+  static bool configured[kMaxDevices] = {};
+  int dev = 0;
+  LP_CUDA_TRY(cudaGetDevice(&dev));
+  if (!configured[dev]) {
+    LP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured[dev] = true;
+  }
+  const int grid = std::max(1, std::min(p.s.num_units, sms));
+  kern<<<grid, NUM_THREADS, smem, st>>>(a, b, o, p);
+  LP_LAUNCH_CHECK("tc_gemm_kernel");
+  return LP_OK;
+}
+
+template <int EPI, bool A_MN, bool B_MN>
+int launch_gemm_cap(bool cap, cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
+                    const GemmParams& p, int sms) {
+  return cap ? launch_gemm<EPI, A_MN, B_MN, true>(st, a, b, o, p, sms)
+             : launch_gemm<EPI, A_MN, B_MN, false>(st, a, b, o, p, sms);
+}
+
+int check_common(const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, const int32_t* y) {
+  if (T < 0 || d <= 0 || Vs <= 0) return fail(LP_EINVAL, "bad sizes T=%lld d=%lld Vs=%lld", (long long)T, (long long)d,
+                                               (long long)Vs);
+  if (T > (int64_t)1 << 30 || Vs > (int64_t)1 << 30) return fail(LP_EINVAL, "T or Vs above 2^30");
+  if (d % 8 != 0) return fail(LP_EINVAL, "hidden size d=%lld must be a multiple of 8", (long long)d);
+  if (ldh < d || ldh % 8 != 0) return fail(LP_EINVAL, "ldh=%lld must be >= d and a multiple of 8", (long long)ldh);
+  if (T > 0 && (H == nullptr || y == nullptr)) return fail(LP_EINVAL, "null hidden or targets");
+  if (W == nullptr) return fail(LP_EINVAL, "null embedding");
+  return LP_OK;
+}
+
+}  // namespace
+
+// ============================================================================= C ABI
+extern "C" {
+
+int lp_version(void) { return 100; }
+
+const char* lp_last_error(void) { return g_last_error.c_str(); }
+
+long long lp_launch_count(void) { return g_launches.load(); }
+
+int lp_device_error(int device, int* code) {
+  int prev = 0;
+  LP_CUDA_TRY(cudaGetDevice(&prev));
+  LP_CUDA_TRY(cudaSetDevice(device));
+  int v = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_lp_device_error, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_lp_device_error, &zero, sizeof(int));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(LP_ECUDA, "lp_device_error: %s", cudaGetErrorString(e));
+  if (code) *code = v;
+  return LP_OK;
+}
+
+size_t lp_fwd_workspace_bytes(int64_t T, int64_t Vs) {
+  DeviceInfo* di = nullptr;
+  int sms = 148;
+  if (current_device_info(&di) == LP_OK) sms = di->sms;
+  if (T <= 0 || Vs <= 0) return 256;
+  GemmSched s = plan_fwd(T, Vs, 64, sms);
+  return align_up((size_t)s.n_groups * T * sizeof(float2), 256) + align_up((size_t)T * 4, 256);
+}
+
+int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
+           const int32_t* y, float softcap, float* stats, float* logp, void* workspace, size_t workspace_bytes) {
+  int rc = check_common(H, T, d, ldh, W, Vs, y);
+  if (rc) return rc;
+  if (T == 0) return LP_OK;
+  if (stats == nullptr) return fail(LP_EINVAL, "null stats");
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device_info(&di))) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  GemmSched s = plan_fwd(T, Vs, d, di->sms);
+  const size_t part_bytes = align_up((size_t)s.n_groups * T * sizeof(float2), 256);
+  const size_t need = part_bytes + align_up((size_t)T * 4, 256);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(LP_EWORKSPACE, "lp_fwd needs %zu workspace bytes, got %zu", need, workspace_bytes);
+  float2* part = reinterpret_cast<float2*>(workspace);
+  float* tgt = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + part_bytes);
+
+  alignas(64) CUtensorMap ta, tb;
+  if ((rc = map_bf16(&ta, H, d, T, ldh, BK, BM, "hidden"))) return rc;
+  if ((rc = map_bf16(&tb, W, d, Vs, d, BK, BN, "embedding"))) return rc;
+  GemmParams p{};
+  p.s = s;
+  p.e.y = y;
+  p.e.v_off = v_off;
+  p.e.softcap = softcap;
+  p.e.part = part;
+  p.e.tgt = tgt;
+  if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di->sms))) return rc;
+  fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, s.n_groups, (int)T, tgt, y, v_off, Vs, stats, logp);
+  LP_LAUNCH_CHECK("fwd_finalize_kernel");
+  return LP_OK;
+}
+
+int lp_combine(void* stream, const float* shard_stats, int P, int64_t T, float* logp, float* norm) {
+  if (P <= 0 || T < 0) return fail(LP_EINVAL, "bad P=%d or T=%lld", P, (long long)T);
+  if (T == 0) return LP_OK;
+  if (shard_stats == nullptr) return fail(LP_EINVAL, "null shard_stats");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  combine_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(shard_stats, P, (int)T, logp, norm);
+  LP_LAUNCH_CHECK("combine_kernel");
+  return LP_OK;
+}
+
+size_t lp_bwd_workspace_bytes(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int flags) {
+  DeviceInfo* di = nullptr;
+  int sms = 148;
+  if (current_device_info(&di) == LP_OK) sms = di->sms;
+  if (T <= 0 || Vs <= 0 || d <= 0) return 256;
+  return bwd_layout(T, d, Vs, token_chunk, flags, sms).total + 256;
+}
+
+int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
+           const int32_t* y, float softcap, const float* norm, const float* g, void* dH, int64_t ld_dh, void* dW,
+           int flags, int64_t token_chunk, void* workspace, size_t workspace_bytes) {
+  int rc = check_common(H, T, d, ldh, W, Vs, y);
+  if (rc) return rc;
+  const bool want_dh = !(flags & LP_BWD_NO_DH), want_dw = !(flags & LP_BWD_NO_DW);
+  const bool dh_f32 = flags & LP_BWD_DH_F32, dw_bf16 = flags & LP_BWD_DW_BF16;
+  if (want_dh && (dH == nullptr || ld_dh < d || ld_dh % 8 != 0))
+    return fail(LP_EINVAL, "dH must be non-null with ld_dh >= d and ld_dh %% 8 == 0");
+  if (want_dw && dW == nullptr) return fail(LP_EINVAL, "null dW");
+  if (T > 0 && (norm == nullptr || g == nullptr)) return fail(LP_EINVAL, "null norm or g");
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device_info(&di))) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (T == 0) {
+    // no tokens: dW is zero
+    if (want_dw) LP_CUDA_TRY(cudaMemsetAsync(dW, 0, (size_t)Vs * d * (dw_bf16 ? 2 : 4), st));
+    return LP_OK;
+  }
+  const BwdLayout L = bwd_layout(T, d, Vs, token_chunk, flags, di->sms);
+  if (workspace == nullptr || workspace_bytes < L.total)
+    return fail(LP_EWORKSPACE, "lp_bwd needs %zu workspace bytes, got %zu", L.total, workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 1023) != 0) return fail(LP_EINVAL, "workspace must be 1024-byte aligned");
+  char* ws = reinterpret_cast<char*>(workspace);
+  __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(ws + L.dz_off);
+  float* part = reinterpret_cast<float*>(ws + L.part_off);
+  float* dw_acc = (want_dw && dw_bf16 && L.chunks > 1) ? reinterpret_cast<float*>(ws + L.dwacc_off)
+                                                        : reinterpret_cast<float*>(dW);
+  const bool cap = softcap > 0.f;
+  const __nv_bfloat16* Hb = reinterpret_cast<const __nv_bfloat16*>(H);
+
+  for (int64_t c = 0; c < L.chunks; ++c) {
+    const int64_t t0 = c * L.tc;
+    const int64_t tcur = std::min<int64_t>(L.tc, T - t0);
+    const __nv_bfloat16* Hc = Hb + t0 * ldh;
+
+    // 1) recompute logits tile by tile and write dZ (bf16) for this chunk
+    {
+      alignas(64) CUtensorMap ta, tb, to;
+      if ((rc = map_bf16(&ta, Hc, d, tcur, ldh, BK, BM, "hidden chunk"))) return rc;
+      if ((rc = map_bf16(&tb, W, d, Vs, d, BK, BN, "embedding"))) return rc;
+      if ((rc = map_bf16(&to, dz, Vs, tcur, L.ldz, 64, 32, "dZ store"))) return rc;
+      GemmParams p{};
+      p.s = plan_gemm(tcur, Vs, d, di->sms, false, 0);
+      p.e.y = y + t0;
+      p.e.v_off = v_off;
+      p.e.softcap = softcap;
+      p.e.g = g + t0;
+      p.e.stats = norm + t0;
+      p.e.stats_ld = T;
+      if ((rc = launch_gemm_cap<EPI_BWD_DZ, false, false>(cap, st, ta, tb, to, p, di->sms))) return rc;
+    }
+    // 2) dH[t0:t0+tcur] = dZ . W
+    if (want_dh) {
+      alignas(64) CUtensorMap ta, tb, to;
+      if ((rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, BK, BM, "dZ as A"))) return rc;
+      if ((rc = map_bf16(&tb, W, d, Vs, d, 64, 64, "embedding as MN-major B"))) return rc;
+      GemmParams p{};
+      p.s = plan_gemm(tcur, d, Vs, di->sms, true, 1);
+      char* dh_c = reinterpret_cast<char*>(dH) + (size_t)t0 * ld_dh * (dh_f32 ? 4 : 2);
+      if (p.s.k_splits == 1) {
+        if (dh_f32) {
+          if ((rc = map_f32(&to, dh_c, d, tcur, ld_dh, 32, 32, "dH store"))) return rc;
+          p.e.store_mode = STORE_F32;
+        } else {
+          if ((rc = map_bf16(&to, dh_c, d, tcur, ld_dh, 64, 32, "dH store"))) return rc;
+          p.e.store_mode = STORE_BF16;
+        }
+        p.e.split_rows = 0;
+      } else {
+        if ((rc = map_f32(&to, part, d, (uint64_t)p.s.k_splits * L.mpad, d, 32, 32, "dH partials"))) return rc;
+        p.e.store_mode = STORE_F32;
+        p.e.split_rows = (int)L.mpad;
+      }
+      if ((rc = launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di->sms))) return rc;
+      if (p.s.k_splits > 1) {
+        const int64_t total = tcur * (d / 4);
+        const unsigned grid = (unsigned)std::min<int64_t>(cdiv(total, 256), (int64_t)di->sms * 8);
+        splitk_reduce_kernel<<<grid, 256, 0, st>>>(part, p.s.k_splits, tcur, d, L.mpad, dh_c, ld_dh, dh_f32 ? 0 : 1);
+        LP_LAUNCH_CHECK("splitk_reduce_kernel");
+      }
+    }
+    // 3) dW (+)= dZ^T . H_chunk
+    if (want_dw) {
+      alignas(64) CUtensorMap ta, tb, to;
+      if ((rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, 64, 64, "dZ as MN-major A"))) return rc;
+      if ((rc = map_bf16(&tb, Hc, d, tcur, ldh, 64, 64, "hidden as MN-major B"))) return rc;
+      GemmParams p{};
+      p.s = plan_gemm(Vs, d, tcur, di->sms, false, 1);
+      const bool direct_bf16 = dw_bf16 && L.chunks == 1;
+      if (direct_bf16) {
+        if ((rc = map_bf16(&to, dW, d, Vs, d, 64, 32, "dW store"))) return rc;
+        p.e.store_mode = STORE_BF16;
+      } else {
+        if ((rc = map_f32(&to, dw_acc, d, Vs, d, 32, 32, "dW store"))) return rc;
+        p.e.store_mode = c == 0 ? STORE_F32 : STORE_F32_ADD;
+      }
+      if ((rc = launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di->sms))) return rc;
+    }
+  }
+  if (want_dw && dw_bf16 && L.chunks > 1) {
+    const int64_t n = Vs * d;
+    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n / 4 + 1, 256), (int64_t)di->sms * 8);
+    f32_to_bf16_kernel<<<grid, 256, 0, st>>>(dw_acc, reinterpret_cast<__nv_bfloat16*>(dW), n);
+    LP_LAUNCH_CHECK("f32_to_bf16_kernel");
+  }
+  return LP_OK;
+}
+
+int lp_gemm_bf16(void* stream, const void* A, int64_t M, int64_t K, int64_t lda, int a_mn, const void* B, int64_t N,
+                 int64_t ldb, int b_mn, float* D, int64_t ldd) {
+  if (M <= 0 || N <= 0 || K <= 0) return fail(LP_EINVAL, "bad GEMM sizes");
+  if (A == nullptr || B == nullptr || D == nullptr) return fail(LP_EINVAL, "null GEMM operand");
+  if (ldd < N || ldd % 4 != 0) return fail(LP_EINVAL, "ldd must be >= N and a multiple of 4");
+  if (N % 4 != 0) return fail(LP_EINVAL, "N must be a multiple of 4");
+  DeviceInfo* di = nullptr;
+  int rc = current_device_info(&di);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  alignas(64) CUtensorMap ta, tb, to;
+  // K-major A: [M rows][K], MN-major A: [K rows][M]; likewise B with N.
+  if (a_mn) rc = map_bf16(&ta, A, M, K, lda, 64, 64, "A (MN-major)");
+  else rc = map_bf16(&ta, A, K, M, lda, BK, BM, "A (K-major)");
+  if (rc) return rc;
+  if (b_mn) rc = map_bf16(&tb, B, N, K, ldb, 64, 64, "B (MN-major)");
+  else rc = map_bf16(&tb, B, K, N, ldb, BK, BN, "B (K-major)");
+  if (rc) return rc;
+  if ((rc = map_f32(&to, D, N, M, ldd, 32, 32, "D"))) return rc;
+  GemmParams p{};
+  p.s = plan_gemm(M, N, K, di->sms, false, 0);
+  p.e.store_mode = STORE_F32;
+  if (!a_mn && !b_mn) return launch_gemm<EPI_STORE, false, false, false>(st, ta, tb, to, p, di->sms);
+  if (!a_mn && b_mn) return launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di->sms);
+  if (a_mn && b_mn) return launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di->sms);
+  return launch_gemm<EPI_STORE, true, false, false>(st, ta, tb, to, p, di->sms);
+}
+
+size_t lp_compact_workspace_bytes(int64_t B, int64_t N) {
+  const int64_t slots = std::max<int64_t>(B * N, 1);
+  return align_up((size_t)cdiv(slots, kCompactBlock) * 4, 256) * 2;
+}
+
+int lp_compact(void* stream, const uint8_t* mask, int64_t B, int64_t N, const void* hidden, int64_t hidden_bstride,
+               int64_t hidden_rstride, int64_t row_offset, int64_t d, const int32_t* ids, void* H_out, int32_t* y_out,
+               int32_t* idx, int32_t* pos, int32_t* count, void* workspace, size_t workspace_bytes) {
+  if (B < 0 || N < 0) return fail(LP_EINVAL, "bad B=%lld N=%lld", (long long)B, (long long)N);
+  const int64_t slots = B * N;
+  if (slots > ((int64_t)1 << 31) - 1) return fail(LP_EINVAL, "too many slots");
+  if (mask == nullptr || idx == nullptr || pos == nullptr || count == nullptr)
+    return fail(LP_EINVAL, "null mask / idx / pos / count");
+  if (hidden != nullptr) {
+    if (d <= 0 || d % 8 != 0) return fail(LP_EINVAL, "d=%lld must be a positive multiple of 8", (long long)d);
+    if (H_out == nullptr) return fail(LP_EINVAL, "null H_out");
+    if (hidden_rstride % 8 != 0 || hidden_bstride % 8 != 0) return fail(LP_EINVAL, "hidden strides must be multiples of 8");
+    if ((reinterpret_cast<uintptr_t>(hidden) & 15) || (reinterpret_cast<uintptr_t>(H_out) & 15))
+      return fail(LP_EINVAL, "hidden / H_out must be 16-byte aligned");
+    if (y_out != nullptr && ids == nullptr) return fail(LP_EINVAL, "y_out needs ids");
+  }
+  const size_t need = lp_compact_workspace_bytes(B, N);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(LP_EWORKSPACE, "lp_compact needs %zu workspace bytes, got %zu", need, workspace_bytes);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (slots == 0) {
+    LP_CUDA_TRY(cudaMemsetAsync(count, 0, sizeof(int32_t), st));
+    return LP_OK;
+  }
+  const int nblocks = (int)cdiv(slots, kCompactBlock);
+  int* block_counts = reinterpret_cast<int*>(workspace);
+  int* block_offsets = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + need / 2);
+  compact_count_kernel<<<nblocks, 256, 0, st>>>(mask, slots, block_counts);
+  LP_LAUNCH_CHECK("compact_count_kernel");
+  compact_scan_kernel<<<1, 1024, 0, st>>>(block_counts, nblocks, block_offsets, count);
+  LP_LAUNCH_CHECK("compact_scan_kernel");
+  compact_write_kernel<<<nblocks, 256, 0, st>>>(mask, slots, block_offsets, idx, pos);
+  LP_LAUNCH_CHECK("compact_write_kernel");
+  if (hidden != nullptr) {
+    DeviceInfo* di = nullptr;
+    int rc = current_device_info(&di);
+    if (rc) return rc;
+    const int64_t warps = std::min<int64_t>(slots, (int64_t)di->sms * 32);
+    compact_gather_kernel<<<(unsigned)cdiv(warps * 32, 256), 256, 0, st>>>(
+        idx, count, N, reinterpret_cast<const __nv_bfloat16*>(hidden), hidden_bstride, hidden_rstride, row_offset, d,
+        ids, reinterpret_cast<__nv_bfloat16*>(H_out), y_out);
+    LP_LAUNCH_CHECK("compact_gather_kernel");
+  }
+  return LP_OK;
+}
+
+int lp_scatter_rows(void* stream, const void* src, int64_t src_stride, const int32_t* pos, int64_t slots,
+                    int64_t width, int elem_bytes, void* out, int64_t out_stride, int64_t rows_per_group,
+                    int64_t group_stride) {
+  if (slots < 0 || width <= 0 || (elem_bytes != 2 && elem_bytes != 4))
+    return fail(LP_EINVAL, "bad slots / width / elem_bytes");
+  if (rows_per_group <= 0) return fail(LP_EINVAL, "rows_per_group must be positive");
+  if (slots == 0) return LP_OK;
+  if (src == nullptr || pos == nullptr || out == nullptr) return fail(LP_EINVAL, "null src / pos / out");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t row_bytes = width * elem_bytes;
+  const bool vec = row_bytes % 16 == 0 && (src_stride * elem_bytes) % 16 == 0 && (out_stride * elem_bytes) % 16 == 0 &&
+                   (group_stride * elem_bytes) % 16 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  if (vec) {
+    const int64_t warps = std::min<int64_t>(slots, 148 * 64);
+    scatter_rows_vec_kernel<<<(unsigned)cdiv(warps * 32, 256), 256, 0, st>>>(
+        reinterpret_cast<const uint8_t*>(src), src_stride * elem_bytes, pos, slots, row_bytes,
+        reinterpret_cast<uint8_t*>(out), out_stride * elem_bytes, rows_per_group, group_stride * elem_bytes);
+    LP_LAUNCH_CHECK("scatter_rows_vec_kernel");
+  } else {
+    const int64_t total = slots * width;
+    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(total, 256), 148 * 16);
+    scatter_rows_elem_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const uint8_t*>(src), src_stride, pos, slots,
+                                                   width, elem_bytes, reinterpret_cast<uint8_t*>(out), out_stride,
+                                                   rows_per_group, group_stride);
+    LP_LAUNCH_CHECK("scatter_rows_elem_kernel");
+  }
+  return LP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,486 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a with pluggable epilogues.
+//
+//   D[M, N] = A[M, K] . B[N, K]^T       (bf16 operands, f32 accumulation in TMEM)
+//
+// One CTA per SM walks a static round-robin list of work units. A unit is one 128-row
+// M tile, a run of consecutive 256-column N tiles and a range of 64-deep K blocks.
+//
+//   warp 0      : TMA producer (one thread) -> NUM_STAGES-deep smem ring (48 KB / stage)
+//   warp 1      : TMEM allocator + MMA issuer (one thread), tcgen05.mma M=128 N=256 K=16
+//   warps 2..5  : epilogue; warp w reads TMEM lanes 32*(w%4).. (its 32 rows of the tile)
+//
+// The two 128x256 f32 accumulators (512 TMEM columns) are double-buffered, so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Operands are either K-major (rows of the tile contiguous along K) or MN-major
+// (contiguous along M / N); both are staged by TMA with 128-byte swizzle.
+//
+// Epilogues:
+//   EPI_FWD_LSE : softcap + running (max, sum-exp) per row in base 2 + target pick, never
+//                 writing logits; one (max, sum) partial per row per unit.
+//   EPI_BWD_DZ  : recompute path; dZ = g * (onehot - softmax) * softcap' written as bf16
+//                 through swizzled smem staging + TMA store.
+//   EPI_STORE   : plain f32 / bf16 store or f32 TMA reduce-add of the accumulator.
+#pragma once
+
+#include "lp_ptx.cuh"
+
+namespace lpk {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int NUM_STAGES = 4;
+constexpr int EPI_WARPS = 4;
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int STAGING_BUF_BYTES = 32 * 128;                 // 32 rows x 128 B, one TMA box
+constexpr int STAGING_WARP_BYTES = 2 * STAGING_BUF_BYTES;  // double-buffered per warp
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+enum : int { EPI_FWD_LSE = 0, EPI_BWD_DZ = 1, EPI_STORE = 2 };
+enum : int { STORE_BF16 = 0, STORE_F32 = 1, STORE_F32_ADD = 2 };
+
+struct GemmSched {
+  int M, N, K;
+  int tiles_m, tiles_n, k_blocks;
+  int n_group, n_groups;  // N tiles per unit, number of N groups
+  int k_splits, kb_per_split;
+  int num_units;
+  int n_fast;  // 1: consecutive units step through N groups first (share the A tile)
+};
+
+struct EpiParams {
+  const int32_t* y;      // [M] target ids (global vocabulary ids)
+  long long v_off;       // first vocabulary id held by this shard
+  float softcap;         // <= 0 means no softcap
+  float2* part;          // FWD: [n_groups][M] (running max in base 2, running sum)
+  float* tgt;            // FWD: [M] target logit (natural units), written by the owning tile
+  const float* g;        // DZ : [M] upstream d logp
+  const float* stats;    // DZ : [2][stats_ld] global (max, sum) in natural units
+  long long stats_ld;    // DZ : row stride of stats
+  int store_mode;        // STORE: STORE_BF16 / STORE_F32 / STORE_F32_ADD
+  int split_rows;        // STORE: output-row offset between K splits (partials)
+};
+
+struct GemmParams {
+  GemmSched s;
+  EpiParams e;
+};
+
+struct Unit {
+  int m_tile, group, split;
+  int n_begin, n_count;
+  int kb_begin, kb_count;
+};
+
+__device__ __forceinline__ Unit get_unit(const GemmSched& s, int u) {
+  int m, g, ks;
+  if (s.n_fast) {
+    g = u % s.n_groups;
+    const int r = u / s.n_groups;
+    m = r % s.tiles_m;
+    ks = r / s.tiles_m;
+  } else {
+    m = u % s.tiles_m;
+    const int r = u / s.tiles_m;
+    g = r % s.n_groups;
+    ks = r / s.n_groups;
+  }
+  Unit x;
+  x.m_tile = m;
+  x.group = g;
+  x.split = ks;
+  x.n_begin = g * s.n_group;
+  x.n_count = min(s.n_group, s.tiles_n - x.n_begin);
+  x.kb_begin = ks * s.kb_per_split;
+  x.kb_count = min(s.kb_per_split, s.k_blocks - x.kb_begin);
+  return x;
+}
+
+template <int EPI>
+__host__ __device__ constexpr int staging_bytes() {
+  return EPI == EPI_FWD_LSE ? 0 : EPI_WARPS * STAGING_WARP_BYTES;
+}
+
+template <int EPI>
+__host__ __device__ constexpr int gemm_smem_bytes() {
+  // 1 KB alignment slack + stages + staging + 16 barriers + tmem slot + abort flag
+  return 1024 + NUM_STAGES * STAGE_BYTES + staging_bytes<EPI>() + 256;
+}
+
+// Swizzled byte offset of 16-byte chunk c of row r inside a 128B-swizzled, 1 KB aligned box.
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+// ----------------------------------------------------------------------------- kernel
+template <int EPI, bool A_MN, bool B_MN, bool HAS_CAP>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmO, const GemmParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint8_t* staging = smem + NUM_STAGES * STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + staging_bytes<EPI>());
+  uint64_t* full_bar = bars;                    // [NUM_STAGES] TMA -> MMA
+  uint64_t* empty_bar = bars + NUM_STAGES;      // [NUM_STAGES] MMA -> TMA
+  uint64_t* tfull_bar = bars + 2 * NUM_STAGES;  // [2] MMA -> epilogue
+  uint64_t* tempty_bar = tfull_bar + 2;         // [2] epilogue -> MMA
+  uint64_t* done_bar = tempty_bar + 2;          // [1] MMA drain on exit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const GemmSched& S = P.s;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NUM_STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], EPI_WARPS);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (EPI != EPI_FWD_LSE) prefetch_tmap(&tmO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int last_stage_phase[NUM_STAGES];
+#pragma unroll
+      for (int s = 0; s < NUM_STAGES; ++s) last_stage_phase[s] = -1;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < S.num_units; u += gridDim.x) {
+        const Unit un = get_unit(S, u);
+        for (int nt = un.n_begin; ok && nt < un.n_begin + un.n_count; ++nt) {
+          for (int kb = un.kb_begin; kb < un.kb_begin + un.kb_count; ++kb, ++it) {
+            const int s = it % NUM_STAGES;
+            const uint32_t ph = (it / NUM_STAGES) & 1;
+            if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, DEV_TIMEOUT_PRODUCER)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+            last_stage_phase[s] = (int)ph;
+            uint8_t* a = stages + s * STAGE_BYTES;
+            uint8_t* b = a + A_STAGE_BYTES;
+            const int k0 = kb * BK;
+            if (!A_MN) {
+              tma_load_2d(a, &tmA, &full_bar[s], k0, un.m_tile * BM);
+            } else {
+              tma_load_2d(a, &tmA, &full_bar[s], un.m_tile * BM, k0);
+              tma_load_2d(a + 8192, &tmA, &full_bar[s], un.m_tile * BM + 64, k0);
+            }
+            if (!B_MN) {
+              tma_load_2d(b, &tmB, &full_bar[s], k0, nt * BN);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) tma_load_2d(b + 8192 * j, &tmB, &full_bar[s], nt * BN + 64 * j, k0);
+            }
+          }
+        }
+      }
+      // Never leave with TMA writes in flight into this CTA's shared memory.
+      for (int s = 0; s < NUM_STAGES; ++s) {
+        if (last_stage_phase[s] < 0) continue;
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_bar[s], (uint32_t)last_stage_phase[s])) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(DEV_TIMEOUT_DRAIN);
+            break;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < S.num_units; u += gridDim.x) {
+        const Unit un = get_unit(S, u);
+        for (int nt = un.n_begin; ok && nt < un.n_begin + un.n_count; ++nt, ++tc) {
+          const int buf = tc & 1;
+          const uint32_t tph = (tc >> 1) & 1;
+          if (!mbar_wait_bounded(&tempty_bar[buf], tph ^ 1, abort_flag, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+          for (int kb = 0; kb < un.kb_count; ++kb, ++it) {
+            const int s = it % NUM_STAGES;
+            const uint32_t ph = (it / NUM_STAGES) & 1;
+            if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, DEV_TIMEOUT_MMA)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(stages + s * STAGE_BYTES);
+            const uint32_t b_addr = a_addr + A_STAGE_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t ad =
+                  A_MN ? smem_desc_sw128(a_addr + kk * 2048, 8192, 1024) : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+              const uint64_t bd =
+                  B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024) : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+              mma_bf16_ss(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(&empty_bar[s]);  // frees the smem stage once these MMAs have read it
+          }
+          if (!ok) break;
+          mma_commit(&tfull_bar[buf]);  // accumulator ready for the epilogue
+        }
+      }
+      // Drain: every MMA issued by this thread completes before TMEM is released.
+      mma_commit(done_bar);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(done_bar, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          record_device_error(DEV_TIMEOUT_DRAIN);
+          break;
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue warps
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint8_t* my_staging = staging + ew * STAGING_WARP_BYTES;
+    int sb = 0;
+    uint32_t tc = 0;
+    const EpiParams& E = P.e;
+    const float cap = E.softcap;
+    const float k1 = HAS_CAP ? 2.0f * kLog2e / cap : 0.f;  // x -> 2x/c in base 2
+    const float c2 = HAS_CAP ? cap * kLog2e : 0.f;        // c in base 2
+    bool ok = true;
+
+    for (int u = blockIdx.x; ok && u < S.num_units; u += gridDim.x) {
+      const Unit un = get_unit(S, u);
+      const int row = un.m_tile * BM + q * 32 + lane;
+      const bool row_ok = row < S.M;
+
+      // per-row state
+      int yl = -1;
+      float run_m = -INFINITY, run_s = 0.f;
+      float gv = 0.f, l2 = 0.f;
+      if (EPI == EPI_FWD_LSE) {
+        if (row_ok) {
+          const long long t = (long long)E.y[row] - E.v_off;
+          yl = (t >= 0 && t < (long long)S.N) ? (int)t : -1;
+        }
+      } else if (EPI == EPI_BWD_DZ) {
+        if (row_ok) {
+          const long long t = (long long)E.y[row] - E.v_off;
+          yl = (t >= 0 && t < (long long)S.N) ? (int)t : -1;
+          gv = E.g[row];
+          l2 = E.stats[row] * kLog2e + log2f(E.stats[E.stats_ld + row]);
+        }
+      }
+
+      for (int nt = un.n_begin; nt < un.n_begin + un.n_count; ++nt, ++tc) {
+        const int buf = tc & 1;
+        const uint32_t tph = (tc >> 1) & 1;
+        // warp-uniform decision: tcgen05.ld below is .sync.aligned
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&tfull_bar[buf], tph, abort_flag, DEV_TIMEOUT_EPILOGUE))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + lane_base + (uint32_t)(buf * BN);
+
+        if constexpr (EPI == EPI_FWD_LSE) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld32(taddr + c * 32, r);
+            tmem_wait_ld(r);
+            const int col0 = nt * BN + c * 32;
+            const int nvalid = S.N - col0;  // columns >= nvalid are vocabulary padding
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float x = __uint_as_float(r[j]);
+              float z = HAS_CAP ? fmaf(-2.f * c2, fast_rcp(1.f + fast_ex2(x * k1)), c2) : x * kLog2e;
+              z = (j < nvalid) ? z : -INFINITY;
+              r[j] = __float_as_uint(z);
+              if (j & 1) mx1 = fmaxf(mx1, z); else mx0 = fmaxf(mx0, z);
+            }
+            const int tj = yl - col0;
+            if ((unsigned)tj < 32u) {
+              float tv = 0.f;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) tv = (j == tj) ? __uint_as_float(r[j]) : tv;
+              E.tgt[row] = tv * kLn2;
+            }
+            const float nm = fmaxf(run_m, fmaxf(mx0, mx1));
+            const float scale = (nm == run_m) ? 1.f : fast_ex2(run_m - nm);
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              s0 += fast_ex2(__uint_as_float(r[j + 0]) - nm);
+              s1 += fast_ex2(__uint_as_float(r[j + 1]) - nm);
+              s2 += fast_ex2(__uint_as_float(r[j + 2]) - nm);
+              s3 += fast_ex2(__uint_as_float(r[j + 3]) - nm);
+            }
+            run_s = fmaf(run_s, scale, (s0 + s1) + (s2 + s3));
+            run_m = nm;
+          }
+        } else if constexpr (EPI == EPI_BWD_DZ) {
+#pragma unroll 1
+          for (int pc = 0; pc < BN / 64; ++pc) {
+            uint32_t r0[32], r1[32];
+            __syncwarp();
+            tmem_ld32(taddr + pc * 64, r0);
+            tmem_ld32(taddr + pc * 64 + 32, r1);
+            tmem_wait_ld2(r0, r1);
+            const int col0 = nt * BN + pc * 64;
+            const int tj = yl - col0;
+            // dZ = g * (onehot - 2^(z2 - l2)) * (1 - tanh^2); packed to bf16 pairs in place
+            uint32_t pk[32];
+#pragma unroll
+            for (int j = 0; j < 64; j += 2) {
+              float v[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int jj = j + h;
+                const float x = __uint_as_float(jj < 32 ? r0[jj] : r1[jj - 32]);
+                float z, chain;
+                if (HAS_CAP) {
+                  const float rr = fast_rcp(1.f + fast_ex2(x * k1));
+                  z = fmaf(-2.f * c2, rr, c2);
+                  chain = 4.f * rr * (1.f - rr);
+                } else {
+                  z = x * kLog2e;
+                  chain = 1.f;
+                }
+                const float p = fast_ex2(z - l2);
+                const float onehot = (jj == tj) ? 1.f : 0.f;
+                v[h] = gv * chain * (onehot - p);
+              }
+              pk[j >> 1] = pack_bf16x2(v[0], v[1]);
+            }
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+            uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
+            const uint32_t sbase = smem_u32(buf_s);
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              st_shared_v4(sbase + sw128_offset(lane, c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmO, buf_s, col0, un.m_tile * BM + q * 32);
+              bulk_commit();
+            }
+            sb ^= 1;
+          }
+        } else {  // EPI_STORE
+          const int row0 = un.split * E.split_rows + un.m_tile * BM + q * 32;
+          if (E.store_mode == STORE_BF16) {
+#pragma unroll 1
+            for (int pc = 0; pc < BN / 64; ++pc) {
+              uint32_t r0[32], r1[32];
+              tmem_ld32(taddr + pc * 64, r0);
+              tmem_ld32(taddr + pc * 64 + 32, r1);
+              tmem_wait_ld2(r0, r1);
+              uint32_t pk[32];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(r0[2 * j]), __uint_as_float(r0[2 * j + 1]));
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                pk[16 + j] = pack_bf16x2(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1]));
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
+              uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
+              const uint32_t sbase = smem_u32(buf_s);
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                st_shared_v4(sbase + sw128_offset(lane, c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmO, buf_s, nt * BN + pc * 64, row0);
+                bulk_commit();
+              }
+              sb ^= 1;
+            }
+          } else {
+#pragma unroll 1
+            for (int pc = 0; pc < BN / 32; ++pc) {
+              uint32_t r[32];
+              tmem_ld32(taddr + pc * 32, r);
+              tmem_wait_ld(r);
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
+              uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
+              const uint32_t sbase = smem_u32(buf_s);
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                st_shared_v4(sbase + sw128_offset(lane, c), r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                if (E.store_mode == STORE_F32_ADD)
+                  tma_reduce_add_2d(&tmO, buf_s, nt * BN + pc * 32, row0);
+                else
+                  tma_store_2d(&tmO, buf_s, nt * BN + pc * 32, row0);
+                bulk_commit();
+              }
+              sb ^= 1;
+            }
+          }
+        }
+
+        // hand the accumulator back to the MMA warp
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[buf]);
+      }
+      if (!ok) break;
+
+      if constexpr (EPI == EPI_FWD_LSE) {
+        if (row_ok) E.part[(size_t)un.group * S.M + row] = make_float2(run_m, run_s);
+      }
+    }
+    if (EPI != EPI_FWD_LSE) {
+      if (lane == 0) bulk_wait<0>();  // all TMA stores of this warp complete before exit
+      __syncwarp();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace lpk

@@ -1,0 +1,244 @@
+// Small HBM-bound kernels around the tensor-core GEMMs: forward finalisation, the
+// cross-shard combine, split-K reduction, f32 -> bf16 conversion, and the response-token
+// compaction (warp-ballot scan + row gather) with its scatter back to the slot layout.
+#pragma once
+
+#include "lp_ptx.cuh"
+
+namespace lpk {
+
+// Merge the per-unit (max2, sum) partials of every vocab group of one shard.
+//   stats[0][t] = max (natural units), stats[1][t] = sum exp(z - max),
+//   stats[2][t] = owned target logit or 0;  logp[t] = stats[2] - (max + log sum)
+__global__ void fwd_finalize_kernel(const float2* __restrict__ part, int n_groups, int T,
+                                    const float* __restrict__ tgt_ws, const int32_t* __restrict__ y, long long v_off,
+                                    long long Vs, float* __restrict__ stats, float* __restrict__ logp) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  float m = -INFINITY;
+  for (int g = 0; g < n_groups; ++g) m = fmaxf(m, part[(size_t)g * T + t].x);
+  float s = 0.f;
+  for (int g = 0; g < n_groups; ++g) {
+    const float2 p = part[(size_t)g * T + t];
+    s += p.y * exp2f(p.x - m);
+  }
+  const long long local = (long long)y[t] - v_off;
+  const bool owned = local >= 0 && local < Vs;
+  const float tgt = owned ? tgt_ws[t] : 0.f;
+  const float mx = m * kLn2;
+  stats[t] = mx;
+  stats[(size_t)T + t] = s;
+  stats[(size_t)2 * T + t] = tgt;
+  if (logp != nullptr) logp[t] = tgt - (mx + logf(s));
+}
+
+// Cross-shard combine: global max, rescaled sum, summed owned target logit.
+__global__ void combine_kernel(const float* __restrict__ shard_stats, int P, int T, float* __restrict__ logp,
+                               float* __restrict__ norm) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  float m = -INFINITY;
+  for (int p = 0; p < P; ++p) m = fmaxf(m, shard_stats[((size_t)p * 3 + 0) * T + t]);
+  float s = 0.f, tgt = 0.f;
+  for (int p = 0; p < P; ++p) {
+    s += shard_stats[((size_t)p * 3 + 1) * T + t] * expf(shard_stats[((size_t)p * 3 + 0) * T + t] - m);
+    tgt += shard_stats[((size_t)p * 3 + 2) * T + t];
+  }
+  if (logp != nullptr) logp[t] = tgt - m - logf(s);
+  if (norm != nullptr) {
+    norm[t] = m;
+    norm[(size_t)T + t] = s;
+  }
+}
+
+// out[r][c] = sum_s part[s][r][c] for r < M, c < N (N % 4 == 0); bf16 or f32 output.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int S, long long M, long long N, long long Mpad,
+                                     void* __restrict__ out, long long ld_out, int out_bf16) {
+  const long long n4 = N / 4;
+  const long long total = M * n4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / n4, c = (i % n4) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < S; ++s) {
+      const float4 v = *reinterpret_cast<const float4*>(part + ((size_t)s * Mpad + r) * N + c);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if (out_bf16) {
+      uint2 pk;
+      pk.x = pack_bf16x2(acc.x, acc.y);
+      pk.y = pack_bf16x2(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + r * ld_out + c) = pk;
+    } else {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + r * ld_out + c) = acc;
+    }
+  }
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, long long n) {
+  const long long n4 = n / 4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(src)[i];
+    uint2 pk;
+    pk.x = pack_bf16x2(v.x, v.y);
+    pk.y = pack_bf16x2(v.z, v.w);
+    reinterpret_cast<uint2*>(dst)[i] = pk;
+  }
+  const long long tail = n4 * 4 + blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (tail < n) dst[tail] = __float2bfloat16_rn(src[tail]);
+}
+
+// ----------------------------------------------------------------------------- compaction
+constexpr int kCompactBlock = 1024;  // slots per block (256 threads x 4)
+
+__global__ void compact_count_kernel(const uint8_t* __restrict__ mask, long long slots, int* __restrict__ block_counts) {
+  __shared__ int warp_sums[8];
+  const long long base = (long long)blockIdx.x * kCompactBlock;
+  int c = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const long long s = base + k * 256 + threadIdx.x;
+    c += (s < slots && mask[s] != 0) ? 1 : 0;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < 8; ++w) t += warp_sums[w];
+    block_counts[blockIdx.x] = t;
+  }
+}
+
+// Exclusive scan of the per-block counts by a single 1024-thread block (warp shuffles).
+__global__ void compact_scan_kernel(const int* __restrict__ block_counts, int nblocks, int* __restrict__ block_offsets,
+                                    int* __restrict__ count) {
+  __shared__ int warp_tot[32];
+  __shared__ int carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int base = 0; base < nblocks; base += 1024) {
+    const int i = base + threadIdx.x;
+    const int v = i < nblocks ? block_counts[i] : 0;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += n;
+    }
+    if (lane == 31) warp_tot[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int t = warp_tot[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += n;
+      }
+      warp_tot[lane] = t;  // inclusive
+    }
+    __syncthreads();
+    const int warp_off = (w > 0 ? warp_tot[w - 1] : 0);
+    if (i < nblocks) block_offsets[i] = carry + warp_off + x - v;
+    __syncthreads();
+    if (threadIdx.x == 0) carry += warp_tot[31];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *count = carry;
+}
+
+// Writes idx (compact -> slot) and pos (slot -> compact or -1), preserving slot order.
+__global__ void compact_write_kernel(const uint8_t* __restrict__ mask, long long slots,
+                                     const int* __restrict__ block_offsets, int32_t* __restrict__ idx,
+                                     int32_t* __restrict__ pos) {
+  __shared__ int warp_cnt[32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const long long base = (long long)blockIdx.x * kCompactBlock;
+  // 256 threads, 4 passes of 256 consecutive slots; running offset across passes
+  int running = block_offsets[blockIdx.x];
+  for (int k = 0; k < 4; ++k) {
+    const long long s = base + k * 256 + threadIdx.x;
+    const bool valid = s < slots && mask[s] != 0;
+    const unsigned ballot = __ballot_sync(0xffffffffu, valid);
+    if (lane == 0) warp_cnt[w] = __popc(ballot);
+    __syncthreads();
+    int before = 0;
+    for (int j = 0; j < w; ++j) before += warp_cnt[j];
+    int total = before;
+    for (int j = w; j < 8; ++j) total += warp_cnt[j];
+    const int my = running + before + __popc(ballot & ((1u << lane) - 1u));
+    if (s < slots) {
+      pos[s] = valid ? my : -1;
+      if (valid) idx[my] = (int32_t)s;
+    }
+    running += total;
+    __syncthreads();
+  }
+}
+
+// One warp per compact row: H_out[i] = hidden row of slot idx[i], y_out[i] = ids[slot].
+__global__ void compact_gather_kernel(const int32_t* __restrict__ idx, const int* __restrict__ count, long long N,
+                                      const __nv_bfloat16* __restrict__ hidden, long long bstride, long long rstride,
+                                      long long row_offset, long long d, const int32_t* __restrict__ ids,
+                                      __nv_bfloat16* __restrict__ H_out, int32_t* __restrict__ y_out) {
+  const int lane = threadIdx.x & 31;
+  const long long warp_id = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  const int n = *count;
+  const long long vec = d / 8;  // 16-byte vectors per row (d % 8 == 0)
+  for (long long i = warp_id; i < n; i += nwarps) {
+    const long long slot = idx[i];
+    const long long b = slot / N, j = slot % N;
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + b * bstride + (j + row_offset) * rstride);
+    uint4* dst = reinterpret_cast<uint4*>(H_out + i * d);
+    for (long long v = lane; v < vec; v += 32) dst[v] = src[v];
+    if (lane == 0 && y_out != nullptr) y_out[i] = ids[slot];
+  }
+}
+
+// out[s] = pos[s] >= 0 ? src[pos[s]] : 0, one warp per slot row; 16-byte vectors.
+__global__ void scatter_rows_vec_kernel(const uint8_t* __restrict__ src, long long src_stride_b,
+                                        const int32_t* __restrict__ pos, long long slots, long long row_bytes,
+                                        uint8_t* __restrict__ out, long long out_stride_b, long long rows_per_group,
+                                        long long group_stride_b) {
+  const int lane = threadIdx.x & 31;
+  const long long warp_id = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  const long long vec = row_bytes / 16;
+  for (long long s = warp_id; s < slots; s += nwarps) {
+    const int p = pos[s];
+    uint4* dst = reinterpret_cast<uint4*>(out + (s / rows_per_group) * group_stride_b + (s % rows_per_group) * out_stride_b);
+    if (p >= 0) {
+      const uint4* sr = reinterpret_cast<const uint4*>(src + (long long)p * src_stride_b);
+      for (long long v = lane; v < vec; v += 32) dst[v] = sr[v];
+    } else {
+      for (long long v = lane; v < vec; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+// Element-wise fallback layout for rows that are not 16-byte multiples (e.g. logps).
+__global__ void scatter_rows_elem_kernel(const uint8_t* __restrict__ src, long long src_stride,
+                                         const int32_t* __restrict__ pos, long long slots, long long width,
+                                         int elem_bytes, uint8_t* __restrict__ out, long long out_stride,
+                                         long long rows_per_group, long long group_stride) {
+  const long long total = slots * width;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long s = i / width, c = i % width;
+    const int p = pos[s];
+    const long long o = (s / rows_per_group) * group_stride + (s % rows_per_group) * out_stride + c;
+    if (elem_bytes == 4) {
+      const float v = p >= 0 ? reinterpret_cast<const float*>(src)[(long long)p * src_stride + c] : 0.f;
+      reinterpret_cast<float*>(out)[o] = v;
+    } else {
+      const uint16_t v = p >= 0 ? reinterpret_cast<const uint16_t*>(src)[(long long)p * src_stride + c] : (uint16_t)0;
+      reinterpret_cast<uint16_t*>(out)[o] = v;
+    }
+  }
+}
+
+}  // namespace lpk

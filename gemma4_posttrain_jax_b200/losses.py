@@ -1,0 +1,249 @@
+"""The reference's logprob-backend interface, served by the B200 kernels.
+
+``per_token_logps`` keeps the signature, argument meaning and error behaviour of
+``gemma4_posttrain_jax/losses.py:307-343`` and adds ``backend="cuda"``: a
+``torch.autograd.Function`` (the analogue of the reference's ``jax.custom_vjp``,
+``pallas/lm_head_logprob_tpuv4.py:69-94``) whose forward runs ``lp_fwd`` (+ the NCCL
+all-gather and ``lp_combine`` when the vocabulary is sharded) and whose backward runs
+``lp_bwd`` (+ the dH sum over shards). The callers on the path are mirrored too:
+``sft_token_logps`` (the shift of ``losses.py:910-926``) and ``completion_logps`` (the
+response slice of ``losses.py:667-682``, with the padded slots compacted away).
+
+There is no fallback: other backends raise, CPU tensors raise, a missing library raises.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import ops
+from .sharding import VocabMesh, all_gather_stats, all_reduce_sum, vocab_offset
+
+
+def _validate(embed: torch.Tensor, hidden: torch.Tensor, targets: torch.Tensor, vocab_chunk: int, sequence_chunk: int):
+    """The three argument checks of ``losses.py:281-286``, same messages."""
+    if tuple(hidden.shape[:-1]) != tuple(targets.shape):
+        raise ValueError(f"hidden prefix {tuple(hidden.shape[:-1])} does not match targets {tuple(targets.shape)}")
+    if embed.ndim != 2 or hidden.shape[-1] != embed.shape[-1]:
+        raise ValueError(f"incompatible embedding {tuple(embed.shape)} and hidden {tuple(hidden.shape)}")
+    if vocab_chunk <= 0 or sequence_chunk <= 0:
+        raise ValueError("vocab_chunk and sequence_chunk must be positive")
+
+
+def _validate_softcap(softcap: float | None) -> None:
+    if softcap is not None and (not math.isfinite(softcap) or softcap <= 0):
+        raise ValueError("softcap must be finite and positive, or None")
+
+
+class _CudaTokenLogps(torch.autograd.Function):
+    """logp[t] of targets under softcap(H . W^T); grads for W (local shard) and H."""
+
+    @staticmethod
+    def forward(ctx, embed, hidden2d, targets1d, softcap, mesh, token_chunk, stats_out):
+        P = mesh.size if mesh is not None else 1
+        if P > 1:
+            off = vocab_offset(embed.shape[0], mesh)
+            stats, _ = ops.shard_forward(embed, hidden2d, targets1d, softcap, vocab_offset=off, want_logp=False)
+            logp, norm = ops.combine(all_gather_stats(stats, mesh))
+        else:
+            off = 0
+            stats, logp = ops.shard_forward(embed, hidden2d, targets1d, softcap, want_logp=True)
+            norm = stats[:2]
+        if stats_out is not None:
+            stats_out.append(norm)
+        ctx.save_for_backward(embed, hidden2d, targets1d, norm)
+        ctx.softcap = softcap
+        ctx.mesh = mesh
+        ctx.offset = off
+        ctx.token_chunk = token_chunk
+        ctx.mark_non_differentiable(norm)
+        return logp
+
+    @staticmethod
+    def backward(ctx, g):
+        embed, hidden2d, targets1d, norm = ctx.saved_tensors
+        mesh: VocabMesh | None = ctx.mesh
+        P = mesh.size if mesh is not None else 1
+        need_dw, need_dh = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if not (need_dw or need_dh):
+            return None, None, None, None, None, None, None
+        # Shards sum their dH partials in f32 before the single rounding to the hidden dtype.
+        dh_dtype = torch.float32 if (P > 1 or hidden2d.dtype == torch.float32) else torch.bfloat16
+        dH, dW = ops.shard_backward(
+            embed,
+            hidden2d,
+            targets1d,
+            ctx.softcap,
+            norm,
+            g,
+            vocab_offset=ctx.offset,
+            need_dh=need_dh,
+            need_dw=need_dw,
+            dh_dtype=dh_dtype,
+            dw_dtype=embed.dtype if embed.dtype in (torch.bfloat16, torch.float32) else torch.float32,
+            token_chunk=ctx.token_chunk,
+        )
+        if dH is not None and P > 1:
+            all_reduce_sum(dH, mesh)
+        if dH is not None and dH.dtype != hidden2d.dtype:
+            dH = dH.to(hidden2d.dtype)
+        return dW, dH, None, None, None, None, None
+
+
+def per_token_logps(
+    embed_tokens: torch.Tensor,
+    hidden: torch.Tensor,
+    targets: torch.Tensor,
+    *,
+    softcap: float | None,
+    vocab_chunk: int = 8192,
+    sequence_chunk: int = 256,
+    mesh: VocabMesh | None = None,
+    backend: str = "cuda",
+    token_chunk: int | None = None,
+    normalization_out: list | None = None,
+) -> torch.Tensor:
+    """Selected-token log-probabilities without materialising ``[..., vocab]`` logits.
+
+    Same contract as ``gemma4_posttrain_jax/losses.py:307-343``. With a ``mesh`` of size
+    > 1, ``embed_tokens`` is this rank's row block (``V / mesh.size`` rows, the
+    ``P("d", None)`` layout) and ``hidden`` / ``targets`` are replicated; the result is
+    replicated. ``vocab_chunk`` / ``sequence_chunk`` are validated as in the reference;
+    the CUDA kernels tile by 128 tokens x 256 vocabulary rows and stream the whole shard,
+    so results do not depend on them. ``token_chunk`` bounds the backward's dZ scratch.
+    ``normalization_out``, if given, receives the [2, T] (max, sum) statistics of
+    ``_vocab_parallel_logps_and_normalization`` (``losses.py:246-260``).
+    """
+    if backend != "cuda":
+        if backend in ("jax", "pallas"):
+            raise ValueError(
+                f"logprob backend {backend!r} is implemented by gemma4_posttrain_jax itself; this package provides "
+                "backend='cuda'"
+            )
+        raise ValueError(f"unknown logprob backend: {backend}")
+    _validate(embed_tokens, hidden, targets, vocab_chunk, sequence_chunk)
+    _validate_softcap(softcap)
+    if mesh is not None and mesh.size > 1 and mesh.axis_names != ("d",):
+        raise ValueError(f"vocab-parallel mesh needs axis 'd': {mesh.axis_names}")
+    out_shape = targets.shape
+    h2 = hidden.reshape(-1, hidden.shape[-1])
+    y = targets.reshape(-1)
+    if y.numel() == 0:
+        return torch.zeros(out_shape, dtype=torch.float32, device=hidden.device)
+    logp = _CudaTokenLogps.apply(embed_tokens, h2, y, softcap, mesh, token_chunk, normalization_out)
+    return logp.reshape(out_shape)
+
+
+class _CompletionLogps(torch.autograd.Function):
+    """Compacted response-token logprobs; scatters results and dH back to the slot layout."""
+
+    @staticmethod
+    def forward(ctx, embed, hidden, completion_ids, completion_mask, prompt_width, softcap, mesh, token_chunk, num_valid):
+        B, N = completion_mask.shape
+        Hc, yc, idx, pos, count = ops.compact(completion_mask, hidden, completion_ids, row_offset=prompt_width - 1)
+        n = int(count.item()) if num_valid is None else int(num_valid)
+        Hn, yn = Hc[:n], yc[:n]
+        P = mesh.size if mesh is not None else 1
+        off = vocab_offset(embed.shape[0], mesh) if P > 1 else 0
+        if n > 0:
+            if P > 1:
+                stats, _ = ops.shard_forward(embed, Hn, yn, softcap, vocab_offset=off, want_logp=False)
+                logp_c, norm = ops.combine(all_gather_stats(stats, mesh))
+            else:
+                stats, logp_c = ops.shard_forward(embed, Hn, yn, softcap, want_logp=True)
+                norm = stats[:2]
+        else:
+            logp_c = torch.zeros((1,), dtype=torch.float32, device=hidden.device)
+            norm = torch.zeros((2, 0), dtype=torch.float32, device=hidden.device)
+        out = torch.empty((B * N,), dtype=torch.float32, device=hidden.device)
+        ops.scatter_rows(logp_c, pos, out)  # out[s] = logp_c[pos[s]] or 0
+        ctx.save_for_backward(embed, Hn, yn, norm, idx[:n], pos)
+        ctx.meta = (B, N, n, prompt_width, softcap, mesh, off, token_chunk, tuple(hidden.shape), hidden.dtype)
+        return out.reshape(B, N)
+
+    @staticmethod
+    def backward(ctx, g):
+        embed, Hn, yn, norm, idx_n, pos = ctx.saved_tensors
+        B, N, n, prompt_width, softcap, mesh, off, token_chunk, hshape, hdtype = ctx.meta
+        P = mesh.size if mesh is not None else 1
+        need_dw, need_dh = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        dW = dhidden = None
+        if n > 0 and (need_dw or need_dh):
+            gc = torch.empty((n,), dtype=torch.float32, device=g.device)
+            ops.scatter_rows(g.reshape(-1).to(torch.float32).contiguous(), idx_n, gc)  # gc[i] = g[idx[i]]
+            dHc, dW = ops.shard_backward(
+                embed, Hn, yn, softcap, norm, gc, vocab_offset=off, need_dh=need_dh, need_dw=need_dw,
+                dh_dtype=torch.float32 if P > 1 else torch.bfloat16, dw_dtype=embed.dtype, token_chunk=token_chunk,
+            )
+            if dHc is not None:
+                if P > 1:
+                    all_reduce_sum(dHc, mesh)
+                    dHc = dHc.to(torch.bfloat16)
+                dhidden = torch.zeros(hshape, dtype=hdtype, device=g.device)
+                # response slice hidden[:, P-1 : P-1+N] receives dHc at valid slots, 0 elsewhere
+                ops.scatter_rows(dHc, pos, dhidden[:, prompt_width - 1 : prompt_width - 1 + N])
+        if need_dw and dW is None:
+            dW = torch.zeros_like(embed)
+        if need_dh and dhidden is None:
+            dhidden = torch.zeros(hshape, dtype=hdtype, device=g.device)
+        return dW, dhidden, None, None, None, None, None, None, None
+
+
+def completion_logps(
+    embed_tokens: torch.Tensor,
+    hidden: torch.Tensor,
+    completion_ids: torch.Tensor,
+    completion_mask: torch.Tensor,
+    *,
+    prompt_width: int,
+    softcap: float | None,
+    mesh: VocabMesh | None = None,
+    token_chunk: int | None = None,
+    num_valid: int | None = None,
+) -> torch.Tensor:
+    """Response-token logprobs of ``trainer_completion_logps`` (``losses.py:667-682``).
+
+    ``hidden`` is the model output [B, P + N, d]; completion token j of row b is predicted
+    by position ``prompt_width + j - 1``. Only ``completion_mask`` slots are computed
+    (compaction); invalid slots return 0, as ``where(completion_mask, logps, 0)`` does.
+    ``num_valid`` (the mask's popcount, when the caller knows it on the host) avoids one
+    device-to-host read.
+    """
+    if hidden.ndim != 3 or completion_ids.ndim != 2 or completion_mask.shape != completion_ids.shape:
+        raise ValueError("hidden must be [B, S, d] and completion ids / mask [B, N]")
+    if prompt_width < 1 or prompt_width - 1 + completion_ids.shape[1] > hidden.shape[1]:
+        raise ValueError("prompt_width and completion width do not fit the hidden sequence")
+    _validate_softcap(softcap)
+    return _CompletionLogps.apply(
+        embed_tokens, hidden, completion_ids, completion_mask, int(prompt_width), softcap, mesh, token_chunk, num_valid
+    )
+
+
+def sft_token_logps(
+    embed_tokens: torch.Tensor,
+    hidden: torch.Tensor,
+    labels: torch.Tensor,
+    *,
+    softcap: float | None,
+    mesh: VocabMesh | None = None,
+    attention_mask: torch.Tensor | None = None,
+    token_chunk: int | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """SFT next-token logps of ``losses.py:910-926``: returns (logps [B, S-1], loss_mask).
+
+    Targets are ``labels[:, 1:]`` with ``-100`` (and padding) masked to id 0, predicted by
+    ``hidden[:, :-1]``; the masked loss is ``-where(mask, logps, 0).sum() / max(mask.sum(), 1)``.
+    """
+    if labels.ndim != 2 or hidden.ndim != 3 or hidden.shape[:2] != labels.shape:
+        raise ValueError("hidden must be [B, S, d] and labels [B, S]")
+    if labels.shape[1] < 2:
+        raise ValueError("SFT sequences need at least two tokens")
+    targets = labels[:, 1:]
+    mask = targets != -100
+    if attention_mask is not None:
+        mask = mask & attention_mask[:, 1:].to(torch.bool)
+    safe = torch.where(mask, targets, torch.zeros_like(targets)).to(torch.int32)
+    logps = per_token_logps(embed_tokens, hidden[:, :-1], safe, softcap=softcap, mesh=mesh, token_chunk=token_chunk)
+    return logps, mask

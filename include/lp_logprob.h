@@ -1,0 +1,159 @@
+/*
+ * lp_logprob.h — C ABI of the B200 (sm_100a) token-logprob library (liblp_b200.so).
+ *
+ * The library computes, for a tied LM head W[V, d] and hidden states H[T, d] (bf16):
+ *     z[t, v]  = softcap(H[t] . W[v])            softcap(x) = c * tanh(x / c), or x
+ *     logp[t]  = z[t, y_t] - log sum_v exp(z[t, v])
+ * and the vector-Jacobian product of logp with respect to H and W, without ever writing
+ * the [T, V] logits to memory. It replaces the reference's logprob backends
+ * (yixiaoer/gemma4-posttrain-jax):
+ *     gemma4_posttrain_jax/losses.py:72-147   _single_partition_logps   (forward)
+ *     gemma4_posttrain_jax/losses.py:172-260  _vocab_parallel_logps_and_normalization
+ *     gemma4_posttrain_jax/losses.py:307-343  per_token_logps (backend switch)
+ *     gemma4_posttrain_jax/pallas/lm_head_logprob_tpuv4.py:41-94,97-152,216-297
+ *                                               custom_vjp fwd / bwd and the dW kernel
+ * Vocabulary parallelism: each caller process holds one shard W[v_off : v_off + Vs] and
+ * calls lp_fwd on it; the per-shard (max, sum, owned target logit) triples are exchanged
+ * by the caller's collective (NCCL all-gather) and merged by lp_combine.
+ *
+ * Conventions
+ *   - All pointers are device pointers unless stated. `stream` is a cudaStream_t (NULL =
+ *     legacy default stream). Calls only enqueue work; nothing synchronises the host.
+ *   - Every entry point returns LP_OK (0) or a negative LP_E* code; lp_last_error()
+ *     returns a message for the calling thread. No C++ exception crosses this boundary.
+ *   - Buffers are owned by the caller. Scratch memory is a caller-provided `workspace`
+ *     of at least the size the matching *_workspace_bytes() function returns.
+ *   - Requirements checked on every call: bf16 H and W, d % 8 == 0, ldh % 8 == 0,
+ *     16-byte aligned base pointers, an sm_100 device.
+ *   - Kernels never spin without a time limit: a broken pipeline makes the kernel exit
+ *     and record a device error code, read (and cleared) by lp_device_error().
+ */
+#ifndef LP_LOGPROB_H_
+#define LP_LOGPROB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LP_API __attribute__((visibility("default")))
+#else
+#define LP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LP_OK 0
+#define LP_EINVAL (-1)        /* bad argument: shape, alignment, null pointer        */
+#define LP_ECUDA (-2)         /* CUDA runtime / driver error                          */
+#define LP_EWORKSPACE (-3)    /* workspace smaller than *_workspace_bytes() asks for  */
+#define LP_EDEVICE (-4)       /* a kernel recorded a device-side error (timeout)      */
+#define LP_EUNSUPPORTED (-5)  /* not an sm_100 device                                 */
+
+/* lp_bwd flags */
+#define LP_BWD_DH_F32 1  /* dH written as f32 (default: bf16)                   */
+#define LP_BWD_DW_BF16 2 /* dW written as bf16 (default: f32)                   */
+#define LP_BWD_NO_DW 4   /* frozen head: skip dW (fwd + dH only)               */
+#define LP_BWD_NO_DH 8   /* skip dH                                            */
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+LP_API int lp_version(void);
+
+/* Message describing the last error returned on this thread ("" if none). */
+LP_API const char* lp_last_error(void);
+
+/* Number of kernels this library has launched in this process (all devices). */
+LP_API long long lp_launch_count(void);
+
+/* Reads and clears the device-side error code recorded by kernels on `device`
+ * (0 = none; 1..4 = a bounded wait gave up). Synchronises that device. */
+LP_API int lp_device_error(int device, int* code);
+
+/* Scratch bytes lp_fwd needs for T tokens against a shard of Vs rows. */
+LP_API size_t lp_fwd_workspace_bytes(int64_t T, int64_t Vs);
+
+/*
+ * Forward over one vocabulary shard (replaces losses.py:98-147 and the per-shard body of
+ * losses.py:199-248).
+ *   H        bf16 [T, ldh] (first d columns used)          W  bf16 [Vs, d]
+ *   y        int32 [T] global target ids; ids outside [v_off, v_off + Vs) are not owned
+ *   softcap  c > 0 applies c * tanh(x / c); c <= 0 disables it (reference: None)
+ *   stats    f32 [3, T]: shard max, shard sum exp(z - max), owned target logit (0 if not owned)
+ *   logp     f32 [T] or NULL: stats[2] - (stats[0] + log stats[1]); only meaningful when
+ *            the shard is the whole vocabulary (v_off == 0, Vs == V)
+ */
+LP_API int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
+           const int32_t* y, float softcap, float* stats, float* logp, void* workspace, size_t workspace_bytes);
+
+/*
+ * Merge P per-shard triples (replaces the pmax / psum combine of losses.py:219,243-245).
+ *   shard_stats f32 [P, 3, T] (lp_fwd's `stats` of every shard, in shard order)
+ *   logp        f32 [T]       global target log-probability
+ *   norm        f32 [2, T] or NULL: global max and global sum exp(z - max), the
+ *               reference's `normalization` output (losses.py:246-247)
+ */
+LP_API int lp_combine(void* stream, const float* shard_stats, int P, int64_t T, float* logp, float* norm);
+
+/* Scratch bytes lp_bwd needs; token_chunk <= 0 selects the default chunk. */
+LP_API size_t lp_bwd_workspace_bytes(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int flags);
+
+/*
+ * Backward over one vocabulary shard (replaces the AD of losses.py:98-147 / :199-248 and
+ * pallas/lm_head_logprob_tpuv4.py:88-152,216-297). For every token chunk the logits tile
+ * is recomputed, dZ = g * (onehot(y) - softmax(z)) * (1 - tanh^2) formed in registers and
+ * fed to two tensor-core GEMMs:
+ *   dH[T, d]  = dZ . W       (partial over this shard: the caller sums over shards)
+ *   dW[Vs, d] = dZ^T . H     (complete for this shard: no communication)
+ *   norm  f32 [2, T]  global max / sum from lp_combine (or lp_fwd when P == 1)
+ *   g     f32 [T]     upstream d loss / d logp
+ *   dH    bf16 or f32 [T, ld_dh] (LP_BWD_DH_F32), may be NULL with LP_BWD_NO_DH
+ *   dW    f32 or bf16 [Vs, d] (LP_BWD_DW_BF16), may be NULL with LP_BWD_NO_DW
+ */
+LP_API int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
+           const int32_t* y, float softcap, const float* norm, const float* g, void* dH, int64_t ld_dh, void* dW,
+           int flags, int64_t token_chunk, void* workspace, size_t workspace_bytes);
+
+/* Scratch bytes lp_compact needs for B * N response slots. */
+LP_API size_t lp_compact_workspace_bytes(int64_t B, int64_t N);
+
+/*
+ * Response-token compaction (replaces the slice + where of losses.py:667-669,682, which
+ * computes every padded slot): slot s = b * N + j is valid when mask[s] != 0.
+ *   idx    int32 [B * N]  compact row -> slot, valid rows first, slot order preserved
+ *   pos    int32 [B * N]  slot -> compact row, or -1 for invalid slots
+ *   count  int32 [1]      number of valid slots
+ * When `hidden` is non-NULL the valid rows are also gathered:
+ *   H_out[i]  = hidden[b * hidden_bstride + (j + row_offset) * hidden_rstride, 0:d]  (bf16)
+ *   y_out[i]  = ids[slot]
+ * (row_offset = prompt_width - 1 reproduces hidden[:, P-1 : P+N-1].)
+ */
+LP_API int lp_compact(void* stream, const uint8_t* mask, int64_t B, int64_t N, const void* hidden, int64_t hidden_bstride,
+               int64_t hidden_rstride, int64_t row_offset, int64_t d, const int32_t* ids, void* H_out, int32_t* y_out,
+               int32_t* idx, int32_t* pos, int32_t* count, void* workspace, size_t workspace_bytes);
+
+/*
+ * Scatter compact rows back to the slot layout, zero-filling invalid slots:
+ *   row(s)[0:width] = pos[s] >= 0 ? src[pos[s], 0:width] : 0     for s in [0, slots)
+ *   row(s) = out + (s / rows_per_group) * group_stride + (s % rows_per_group) * out_stride
+ * so a strided [B, N, width] view (rows_per_group = N) such as the response slice of a
+ * [B, S, d] gradient is written in place. With pos = a list of source rows it is a row
+ * gather. elem_bytes is 2 (bf16) or 4 (f32); strides are in elements.
+ */
+LP_API int lp_scatter_rows(void* stream, const void* src, int64_t src_stride, const int32_t* pos, int64_t slots,
+                    int64_t width, int elem_bytes, void* out, int64_t out_stride, int64_t rows_per_group,
+                    int64_t group_stride);
+
+/*
+ * Test hook of the tensor-core core (no reference counterpart): D[M, N] = A . B^T in f32,
+ * bf16 operands. a_mn = 0: A is [M, K] row-major (lda >= K); a_mn = 1: A is stored
+ * transposed, [K, M] row-major (lda >= M). Likewise b_mn for B ([N, K] or [K, N]).
+ */
+LP_API int lp_gemm_bf16(void* stream, const void* A, int64_t M, int64_t K, int64_t lda, int a_mn, const void* B, int64_t N,
+                 int64_t ldb, int b_mn, float* D, int64_t ldd);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LP_LOGPROB_H_ */
