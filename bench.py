@@ -1,0 +1,451 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 logprob path (one JSON line on rank 0).
+
+Workload (the metric's configuration): GRPO-shaped response-only
+logprob, forward + backward, tied LM head V=262144, d=2048, bf16, softcap 30. 128
+sequences of 2048 (512 prompt + 1536 response slots), response lengths uniform in
+[64, 1536], so ~102k valid response tokens per step; only those are computed
+(compaction). Upstream dlogp = per-sequence advantage ~ N(0,1) x Bernoulli(0.9) keep.
+The vocabulary is sharded over the N ranks (strong scaling: the global batch is fixed);
+hidden states / targets are replicated as at the reference's shard_map boundary, the
+per-token (max, sum, target) triples are all-gathered and merged, dH partials all-reduced.
+
+A step = one call of the public API (``completion_logps``) + its backward on that batch:
+compaction, fused LM-head GEMM + online LSE, combine, recompute backward into dZ, dH and dW
+tensor-core GEMMs, scatter back. ``value`` has the inputs resident in HBM; ``e2e`` adds the
+host->device copy of the step's inputs (pinned) and the device->host read of the logps.
+
+``--impl reference`` times the CPU restatement of the reference's native path
+(``oracle/``; the reference itself is JAX-only and JAX is not installable here) on this
+host's cores, on bounded samples of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+B, PROMPT, RESP, D, V = 128, 512, 1536, 2048, 262144
+SOFTCAP = 30.0
+SEED = 0
+METRIC = "logprob fwd+bwd tokens/s @V=262144,d=2048 (GRPO response tokens, vocab-sharded)"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
+    p.add_argument("--softcap", type=float, default=SOFTCAP, help="<= 0 disables the softcap")
+    p.add_argument("--batch", type=int, default=B, help="sequences (default: config 2's 128)")
+    p.add_argument("--token-chunk", type=int, default=0, help="backward token chunk (0 = library default)")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            d = json.loads(path.read_text())
+            return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+        except Exception:  # noqa: BLE001
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def make_batch(batch: int, seed: int = SEED):
+    """Seeded synthetic GRPO batch (host numpy for masks / ids / advantages)."""
+    rng = np.random.default_rng(seed)
+    prompt_len = rng.integers(128, PROMPT + 1, size=batch)  # left-padded to 512: does not move the slice
+    resp_len = rng.integers(64, RESP + 1, size=batch)
+    mask = np.arange(RESP)[None, :] < resp_len[:, None]
+    ids = rng.integers(0, V, size=(batch, RESP)).astype(np.int32)
+    adv = rng.normal(size=(batch, 1)).astype(np.float32)
+    keep = rng.random((batch, RESP)) < 0.9
+    g = np.where(mask & keep, adv, 0.0).astype(np.float32)
+    return prompt_len, resp_len, mask, ids, g
+
+
+def config_dict(batch, n_valid, world, softcap):
+    return {
+        "workload": "grpo_response_logprob_fwd_bwd (BASELINE config 2)",
+        "global_batch": batch,
+        "seq_len": PROMPT + RESP,
+        "prompt_width": PROMPT,
+        "response_width": RESP,
+        "valid_tokens": int(n_valid),
+        "hidden": D,
+        "vocab": V,
+        "vocab_per_gpu": V // world,
+        "softcap": softcap if softcap > 0 else None,
+        "parallelism": f"vocab{world}",
+        "l2": "no flush: W shard + hidden exceed the 126 MB L2 (>= 0.8 GB each)",
+    }
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+        "clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, indices):
+        self.indices = indices
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", ",".join(map(str, self.indices))],
+                stdout=self.file, stderr=subprocess.DEVNULL,
+            )
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self):
+        if self.file is None:
+            return None
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(mx)), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU baseline
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:  # noqa: BLE001
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_sample(W_host_f32, H_host, ids, mask, g, tokens, softcap):
+    """Oracle fwd+bwd (float32, the reference's chunking) on the first `tokens` valid slots."""
+    from oracle import logprob_oracle as orc
+
+    b, j = np.nonzero(mask)
+    b, j = b[:tokens], j[:tokens]
+    h = H_host[b, j]
+    t0 = time.perf_counter()
+    orc.fwd_bwd_f32(W_host_f32, h, ids[b, j], g[b, j], softcap=softcap if softcap > 0 else None, vocab_chunk=8192,
+                    sequence_chunk=128)
+    return time.perf_counter() - t0
+
+
+def host_inputs(batch, seed=SEED):
+    """Seeded bf16 inputs drawn on the host (for the reference arm, which has no GPU)."""
+    gen = torch.Generator(device="cpu").manual_seed(seed + 1)
+    W = (torch.randn((V, D), generator=gen) * 0.02).to(torch.bfloat16)
+    gen_h = torch.Generator(device="cpu").manual_seed(seed + 2)
+    H = torch.randn((batch, RESP, D), generator=gen_h).to(torch.bfloat16)
+    return W, H
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    _, _, mask, ids, g = make_batch(args.batch)
+    W, H = host_inputs(args.batch)
+    Wf = W.float().numpy()
+    Hf = H.float().numpy()
+    sample = 64
+    for _ in range(args.warmup):
+        cpu_sample(Wf, Hf, ids, mask, g, sample, args.softcap)
+    secs = [cpu_sample(Wf, Hf, ids, mask, g, sample, args.softcap) for _ in range(args.steps)]
+    per = float(np.mean(secs))
+    value = sample / per
+    cores = blas_threads()
+    n_valid = int(mask.sum())
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": per * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": config_dict(args.batch, n_valid, args.gpus, args.softcap),
+        "impl": "reference",
+        "cpu_baseline": {
+            "value": value,
+            "unit": "tokens/s",
+            "cores": cores,
+            "kind": "port",
+            "sample": f"{sample} valid response tokens per step (fwd+bwd over the full V=262144, d=2048), "
+            "numpy float32 restatement of losses.py:72-147 + its recompute backward",
+        },
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- CUDA arm
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch.distributed as dist
+
+    from gemma4_posttrain_jax_b200 import _lib, build
+    from gemma4_posttrain_jax_b200.losses import completion_logps
+    from gemma4_posttrain_jax_b200.sharding import VocabMesh
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if not _lib.LIB_PATH.exists():
+        build.build()
+    _lib.load()
+    mesh = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        mesh = VocabMesh(None)
+
+    softcap = args.softcap if args.softcap > 0 else None
+    prompt_len, resp_len, mask_np, ids_np, g_np = make_batch(args.batch)
+    n_valid = int(mask_np.sum())
+    vs = V // world
+
+    # inputs: the same seeded draws on every rank; each rank keeps its W row block
+    gen = torch.Generator(device=dev).manual_seed(SEED + 1)
+    W_full = (torch.randn((V, D), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    W = W_full[rank * vs : (rank + 1) * vs].clone().requires_grad_(True)
+    del W_full
+    gen_h = torch.Generator(device=dev).manual_seed(SEED + 2)
+    H = torch.randn((args.batch, RESP, D), generator=gen_h, device=dev).to(torch.bfloat16).requires_grad_(True)
+    ids = torch.from_numpy(ids_np).to(dev)
+    mask = torch.from_numpy(mask_np).to(dev)
+    g = torch.from_numpy(g_np).to(dev)
+    chunk = args.token_chunk or None
+
+    def step(Hx, idsx, maskx, gx):
+        lp = completion_logps(W, Hx, idsx, maskx, prompt_width=1, softcap=softcap, mesh=mesh, token_chunk=chunk,
+                              num_valid=n_valid)
+        dW, dH = torch.autograd.grad(lp, (W, Hx), gx)
+        return lp, dW, dH
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------------------------------------------------------- device-resident timing
+    for _ in range(args.warmup):
+        step(H, ids, mask, g)
+    torch.cuda.synchronize()
+    assert _lib.device_error(local) == 0, "device-side error during warm-up"
+    barrier()
+    torch.cuda.synchronize()
+    _lib.profile_enable(True)
+    launches0 = _lib.launch_count()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(list(range(world))) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step(H, ids, mask, g)
+        stop.record()
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
+    prof = _lib.profile_read()
+    _lib.profile_enable(False)
+    ms = max_over_ranks(start.elapsed_time(stop) / args.steps)
+    value = n_valid / (ms / 1e3)
+    clock_summary = clocks.summary() if rank == 0 else None
+    assert _lib.device_error(local) == 0, "device-side error during the timed region"
+
+    # ---------------------------------------------------------------- end-to-end (host buffers)
+    e2e = None
+    if not args.no_e2e:
+        H_host = H.detach().cpu().pin_memory()
+        ids_host = torch.from_numpy(ids_np).pin_memory()
+        mask_host = torch.from_numpy(mask_np).pin_memory()
+        g_host = torch.from_numpy(g_np).pin_memory()
+        out_host = torch.empty((args.batch, RESP), dtype=torch.float32).pin_memory()
+        H_dev = torch.empty_like(H.detach())
+        ids_dev, mask_dev, g_dev = torch.empty_like(ids), torch.empty_like(mask), torch.empty_like(g)
+        h2d = H_host.nbytes + ids_host.nbytes + mask_host.nbytes + g_host.nbytes
+        d2h = out_host.nbytes
+
+        def e2e_step():
+            H_dev.copy_(H_host, non_blocking=True)
+            ids_dev.copy_(ids_host, non_blocking=True)
+            mask_dev.copy_(mask_host, non_blocking=True)
+            g_dev.copy_(g_host, non_blocking=True)
+            lp, _, _ = step(H_dev.detach().requires_grad_(True), ids_dev, mask_dev, g_dev)
+            out_host.copy_(lp.detach(), non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ems = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        e2e = {"value": n_valid / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems, "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h)}
+
+    # ---------------------------------------------------------------- roofline of the dominant kernel
+    peaks, peak_src = load_peaks()
+    flops_per_step = {
+        "fwd_lse_gemm": 2.0 * n_valid * D * vs,
+        "bwd_dz_gemm": 2.0 * n_valid * D * vs,
+        "bwd_dh_gemm": 2.0 * n_valid * D * vs,
+        "bwd_dw_gemm": 2.0 * n_valid * D * vs,
+    }
+    kernels = {}
+    for name, (tot_ms, cnt) in prof.items():
+        per_launch = tot_ms / max(cnt, 1)
+        entry = {"launches_per_step": cnt / args.steps, "ms_per_step": tot_ms / args.steps, "ms_per_launch": per_launch}
+        if name in flops_per_step:
+            tf = flops_per_step[name] * args.steps / (tot_ms / 1e3) / 1e12
+            entry["tflops"] = tf
+            entry["frac_of_sustained_peak"] = tf / peaks["bf16_tflops_sustained"]
+        kernels[name] = entry
+    gemm_names = [k for k in kernels if k in flops_per_step]
+    dom = max(gemm_names, key=lambda k: kernels[k]["ms_per_step"]) if gemm_names else None
+    roofline = None
+    if dom is not None:
+        cnt = prof[dom][1]
+        flop_per_launch = flops_per_step[dom] * args.steps / max(cnt, 1)
+        achieved = flop_per_launch / (kernels[dom]["ms_per_launch"] / 1e3) / 1e12
+        roofline = {
+            "kernel": dom,
+            "bound": "tensor",
+            "achieved": achieved,
+            "peak": peaks["bf16_tflops_sustained"],
+            "unit": "TFLOP/s",
+            "frac": achieved / peaks["bf16_tflops_sustained"],
+            "traffic": None,
+            "peak_source": f"bf16_tflops_sustained ({peak_src}); kernel runs inside a long step",
+            "flop_per_launch": flop_per_launch,
+        }
+    total_flops = 8.0 * n_valid * D * V
+    step_tflops = total_flops / (ms / 1e3) / 1e12
+
+    # ---------------------------------------------------------------- CPU baseline (rank 0, N = 1)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        Wf = W.detach().float().cpu().numpy()
+        Hf = H.detach().float().cpu().numpy()
+        sample = 64
+        t = cpu_sample(Wf, Hf, ids_np, mask_np, g_np, sample, args.softcap)
+        if t < 4.0:
+            sample = 256
+            t = cpu_sample(Wf, Hf, ids_np, mask_np, g_np, sample, args.softcap)
+        cpu = {"value": sample / t, "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
+               "sample": f"{sample} valid response tokens of this workload, fwd+bwd over V=262144, d=2048 "
+               f"({t:.1f} s), numpy float32 restatement of losses.py:72-147 + recompute backward"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) hidden, N(0,0.02) W, uniform targets)",
+            "config": config_dict(args.batch, n_valid, world, args.softcap),
+            "clocks": clock_summary,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "step_tflops": step_tflops,
+            "step_frac_of_sustained_peak": step_tflops / world / peaks["bf16_tflops_sustained"],
+            "kernels": kernels,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

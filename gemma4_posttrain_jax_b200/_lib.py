@@ -33,6 +33,12 @@ _SIG = {
     "lp_last_error": (ctypes.c_char_p, []),
     "lp_launch_count": (ctypes.c_longlong, []),
     "lp_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "lp_profile_enable": (ctypes.c_int, [ctypes.c_int]),
+    "lp_profile_read": (
+        ctypes.c_int,
+        [ctypes.c_int, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong),
+         ctypes.POINTER(ctypes.c_int)],
+    ),
     "lp_fwd_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
     "lp_fwd": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, ctypes.c_float, _P, _P, _P, ctypes.c_size_t]),
     "lp_combine": (ctypes.c_int, [_P, _P, ctypes.c_int, _I64, _P, _P]),
@@ -99,6 +105,26 @@ def device_error(device: int) -> int:
     code = ctypes.c_int(0)
     check(load().lp_device_error(device, ctypes.byref(code)), "lp_device_error")
     return code.value
+
+
+def profile_enable(on: bool = True) -> None:
+    """Start (or stop) recording per-kernel CUDA-event timings; clears earlier records."""
+    check(load().lp_profile_enable(1 if on else 0), "lp_profile_enable")
+
+
+def profile_read(max_tags: int = 32) -> dict[str, tuple[float, int]]:
+    """{kernel name: (total device ms, launches)} of the launches recorded since enabling."""
+    names = ctypes.create_string_buffer(32 * max_tags)
+    ms = (ctypes.c_double * max_tags)()
+    cnt = (ctypes.c_longlong * max_tags)()
+    n = ctypes.c_int(0)
+    check(load().lp_profile_read(max_tags, names, ms, cnt, ctypes.byref(n)), "lp_profile_read")
+    raw = names.raw
+    out = {}
+    for k in range(n.value):
+        name = raw[32 * k : 32 * k + 32].split(b"\0", 1)[0].decode()
+        out[name] = (float(ms[k]), int(cnt[k]))
+    return out
 
 
 def launch_count() -> int:

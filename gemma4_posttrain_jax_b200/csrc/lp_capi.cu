@@ -9,6 +9,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/lp_logprob.h"
 #include "lp_gemm.cuh"
@@ -20,6 +21,48 @@ using namespace lpk;
 
 thread_local std::string g_last_error;
 std::atomic<long long> g_launches{0};
+
+// Optional per-kernel timing: CUDA events recorded on the launching stream around every
+// kernel this library launches, summed per kernel name by lp_profile_read().
+struct ProfRecord {
+  const char* tag;
+  cudaEvent_t start, stop;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfRecord> g_prof_records;
+std::vector<cudaEvent_t> g_prof_pool;
+
+cudaEvent_t prof_event() {
+  if (!g_prof_pool.empty()) {
+    cudaEvent_t e = g_prof_pool.back();
+    g_prof_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+struct ProfScope {
+  cudaStream_t st;
+  const char* tag;
+  cudaEvent_t start = nullptr;
+  ProfScope(cudaStream_t s, const char* t) : st(s), tag(t) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (g_prof_on) {
+      start = prof_event();
+      cudaEventRecord(start, st);
+    }
+  }
+  ~ProfScope() {
+    if (start == nullptr) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    cudaEvent_t stop = prof_event();
+    cudaEventRecord(stop, st);
+    g_prof_records.push_back({tag, start, stop});
+  }
+};
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -230,7 +273,7 @@ BwdLayout bwd_layout(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int 
 // --------------------------------------------------------------------------- launches
 template <int EPI, bool A_MN, bool B_MN, bool CAP>
 int launch_gemm(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
-                const GemmParams& p, int sms) {
+                const GemmParams& p, int sms, const char* tag) {
   auto kern = tc_gemm_kernel<EPI, A_MN, B_MN, CAP>;
   constexpr int smem = gemm_smem_bytes<EPI>();
   static bool configured[kMaxDevices] = {};
@@ -241,6 +284,7 @@ int launch_gemm(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, con
     configured[dev] = true;
   }
   const int grid = std::max(1, std::min(p.s.num_units, sms));
+  ProfScope prof(st, tag);
   kern<<<grid, NUM_THREADS, smem, st>>>(a, b, o, p);
   LP_LAUNCH_CHECK("tc_gemm_kernel");
   return LP_OK;
@@ -248,9 +292,9 @@ int launch_gemm(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, con
 
 template <int EPI, bool A_MN, bool B_MN>
 int launch_gemm_cap(bool cap, cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
-                    const GemmParams& p, int sms) {
-  return cap ? launch_gemm<EPI, A_MN, B_MN, true>(st, a, b, o, p, sms)
-             : launch_gemm<EPI, A_MN, B_MN, false>(st, a, b, o, p, sms);
+                    const GemmParams& p, int sms, const char* tag) {
+  return cap ? launch_gemm<EPI, A_MN, B_MN, true>(st, a, b, o, p, sms, tag)
+             : launch_gemm<EPI, A_MN, B_MN, false>(st, a, b, o, p, sms, tag);
 }
 
 int check_common(const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, const int32_t* y) {
@@ -274,6 +318,47 @@ int lp_version(void) { return 100; }
 const char* lp_last_error(void) { return g_last_error.c_str(); }
 
 long long lp_launch_count(void) { return g_launches.load(); }
+
+int lp_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (auto& r : g_prof_records) {
+    g_prof_pool.push_back(r.start);
+    g_prof_pool.push_back(r.stop);
+  }
+  g_prof_records.clear();
+  g_prof_on = on != 0;
+  return LP_OK;
+}
+
+int lp_profile_read(int max_tags, char* names, double* total_ms, long long* launches, int* n_tags) {
+  if (max_tags <= 0 || names == nullptr || total_ms == nullptr || launches == nullptr || n_tags == nullptr)
+    return fail(LP_EINVAL, "bad lp_profile_read arguments");
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  int n = 0;
+  std::vector<std::string> tags;
+  for (auto& r : g_prof_records) {
+    LP_CUDA_TRY(cudaEventSynchronize(r.stop));
+    float ms = 0.f;
+    LP_CUDA_TRY(cudaEventElapsedTime(&ms, r.start, r.stop));
+    int k = 0;
+    while (k < n && tags[k] != r.tag) ++k;
+    if (k == n) {
+      if (n == max_tags) continue;
+      tags.push_back(r.tag);
+      total_ms[n] = 0.0;
+      launches[n] = 0;
+      ++n;
+    }
+    total_ms[k] += ms;
+    launches[k] += 1;
+  }
+  for (int k = 0; k < n; ++k) {
+    std::strncpy(names + 32 * k, tags[k].c_str(), 31);
+    names[32 * k + 31] = 0;
+  }
+  *n_tags = n;
+  return LP_OK;
+}
 
 int lp_device_error(int device, int* code) {
   int prev = 0;
@@ -324,7 +409,9 @@ int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
   p.e.softcap = softcap;
   p.e.part = part;
   p.e.tgt = tgt;
-  if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di->sms))) return rc;
+  if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di->sms, "fwd_lse_gemm")))
+    return rc;
+  ProfScope prof(st, "fwd_finalize");
   fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, s.n_groups, (int)T, tgt, y, v_off, Vs, stats, logp);
   LP_LAUNCH_CHECK("fwd_finalize_kernel");
   return LP_OK;
@@ -335,6 +422,7 @@ int lp_combine(void* stream, const float* shard_stats, int P, int64_t T, float* 
   if (T == 0) return LP_OK;
   if (shard_stats == nullptr) return fail(LP_EINVAL, "null shard_stats");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ProfScope prof(st, "combine");
   combine_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(shard_stats, P, (int)T, logp, norm);
   LP_LAUNCH_CHECK("combine_kernel");
   return LP_OK;
@@ -398,7 +486,7 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
       p.e.g = g + t0;
       p.e.stats = norm + t0;
       p.e.stats_ld = T;
-      if ((rc = launch_gemm_cap<EPI_BWD_DZ, false, false>(cap, st, ta, tb, to, p, di->sms))) return rc;
+      if ((rc = launch_gemm_cap<EPI_BWD_DZ, false, false>(cap, st, ta, tb, to, p, di->sms, "bwd_dz_gemm"))) return rc;
     }
     // 2) dH[t0:t0+tcur] = dZ . W
     if (want_dh) {
@@ -422,10 +510,11 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
         p.e.store_mode = STORE_F32;
         p.e.split_rows = (int)L.mpad;
       }
-      if ((rc = launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di->sms))) return rc;
+      if ((rc = launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di->sms, "bwd_dh_gemm"))) return rc;
       if (p.s.k_splits > 1) {
         const int64_t total = tcur * (d / 4);
         const unsigned grid = (unsigned)std::min<int64_t>(cdiv(total, 256), (int64_t)di->sms * 8);
+        ProfScope prof(st, "splitk_reduce");
         splitk_reduce_kernel<<<grid, 256, 0, st>>>(part, p.s.k_splits, tcur, d, L.mpad, dh_c, ld_dh, dh_f32 ? 0 : 1);
         LP_LAUNCH_CHECK("splitk_reduce_kernel");
       }
@@ -445,12 +534,13 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
         if ((rc = map_f32(&to, dw_acc, d, Vs, d, 32, 32, "dW store"))) return rc;
         p.e.store_mode = c == 0 ? STORE_F32 : STORE_F32_ADD;
       }
-      if ((rc = launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di->sms))) return rc;
+      if ((rc = launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di->sms, "bwd_dw_gemm"))) return rc;
     }
   }
   if (want_dw && dw_bf16 && L.chunks > 1) {
     const int64_t n = Vs * d;
     const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n / 4 + 1, 256), (int64_t)di->sms * 8);
+    ProfScope prof(st, "f32_to_bf16");
     f32_to_bf16_kernel<<<grid, 256, 0, st>>>(dw_acc, reinterpret_cast<__nv_bfloat16*>(dW), n);
     LP_LAUNCH_CHECK("f32_to_bf16_kernel");
   }
@@ -479,10 +569,10 @@ int lp_gemm_bf16(void* stream, const void* A, int64_t M, int64_t K, int64_t lda,
   GemmParams p{};
   p.s = plan_gemm(M, N, K, di->sms, false, 0);
   p.e.store_mode = STORE_F32;
-  if (!a_mn && !b_mn) return launch_gemm<EPI_STORE, false, false, false>(st, ta, tb, to, p, di->sms);
-  if (!a_mn && b_mn) return launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di->sms);
-  if (a_mn && b_mn) return launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di->sms);
-  return launch_gemm<EPI_STORE, true, false, false>(st, ta, tb, to, p, di->sms);
+  if (!a_mn && !b_mn) return launch_gemm<EPI_STORE, false, false, false>(st, ta, tb, to, p, di->sms, "gemm");
+  if (!a_mn && b_mn) return launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di->sms, "gemm");
+  if (a_mn && b_mn) return launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di->sms, "gemm");
+  return launch_gemm<EPI_STORE, true, false, false>(st, ta, tb, to, p, di->sms, "gemm");
 }
 
 size_t lp_compact_workspace_bytes(int64_t B, int64_t N) {
@@ -515,6 +605,7 @@ int lp_compact(void* stream, const uint8_t* mask, int64_t B, int64_t N, const vo
     return LP_OK;
   }
   const int nblocks = (int)cdiv(slots, kCompactBlock);
+  ProfScope prof(st, "compact");
   int* block_counts = reinterpret_cast<int*>(workspace);
   int* block_offsets = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + need / 2);
   compact_count_kernel<<<nblocks, 256, 0, st>>>(mask, slots, block_counts);
@@ -546,6 +637,7 @@ int lp_scatter_rows(void* stream, const void* src, int64_t src_stride, const int
   if (src == nullptr || pos == nullptr || out == nullptr) return fail(LP_EINVAL, "null src / pos / out");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int64_t row_bytes = width * elem_bytes;
+  ProfScope prof(st, "scatter_rows");
   const bool vec = row_bytes % 16 == 0 && (src_stride * elem_bytes) % 16 == 0 && (out_stride * elem_bytes) % 16 == 0 &&
                    (group_stride * elem_bytes) % 16 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(out) & 15) == 0;

@@ -66,6 +66,14 @@ LP_API const char* lp_last_error(void);
 /* Number of kernels this library has launched in this process (all devices). */
 LP_API long long lp_launch_count(void);
 
+/* Per-kernel timing (for benchmarks): while enabled, every kernel launch of this library
+ * is bracketed by CUDA events on its stream. Enabling (or disabling) clears the record. */
+LP_API int lp_profile_enable(int on);
+
+/* Sums the recorded launches per kernel name (synchronises on the events):
+ * names: max_tags * 32 chars (NUL-terminated names), total_ms / launches: max_tags each. */
+LP_API int lp_profile_read(int max_tags, char* names, double* total_ms, long long* launches, int* n_tags);
+
 /* Reads and clears the device-side error code recorded by kernels on `device`
  * (0 = none; 1..4 = a bounded wait gave up). Synchronises that device. */
 LP_API int lp_device_error(int device, int* code);

@@ -80,9 +80,12 @@ def _blocked_stats(
     n_voc = math.ceil(vocab_size / vocab_chunk)
     seq_pad = n_seq * sequence_chunk - num_tokens
     voc_pad = n_voc * vocab_chunk - vocab_size
-    h = np.pad(flat_hidden.astype(np.float32), ((0, seq_pad), (0, 0)))
+    h = np.pad(np.asarray(flat_hidden, dtype=np.float32), ((0, seq_pad), (0, 0)))
     t = np.pad(flat_targets.astype(np.int64), ((0, seq_pad),))
-    e = np.pad(embed.astype(np.float32), ((0, voc_pad), (0, 0)))
+    # The reference pads the table to a vocab_chunk multiple (losses.py:106); only the last
+    # block needs the padding, so it is padded block by block instead of copying the table.
+    e = np.asarray(embed, dtype=np.float32)
+    del voc_pad
     tgt_out = np.zeros(n_seq * sequence_chunk, np.float32)
     max_out = np.zeros(n_seq * sequence_chunk, np.float32)
     sum_out = np.zeros(n_seq * sequence_chunk, np.float32)
@@ -102,7 +105,10 @@ def _blocked_stats(
         run_sum = np.zeros(sequence_chunk, np.float32)
         for vb in range(n_voc):
             cols = slice(vb * vocab_chunk, (vb + 1) * vocab_chunk)
-            logits = _softcap(hb @ e[cols].T, softcap)
+            blk = e[cols]
+            if blk.shape[0] < vocab_chunk:
+                blk = np.pad(blk, ((0, vocab_chunk - blk.shape[0]), (0, 0)))
+            logits = _softcap(hb @ blk.T, softcap)
             valid = vb * vocab_chunk + np.arange(vocab_chunk) < vocab_size
             logits = np.where(valid[None, :], logits, np.float32(-np.inf))
             new_max = np.maximum(run_max, logits.max(axis=-1))
@@ -304,10 +310,10 @@ def fwd_bwd_f32(
     plus the target-gather term. Returns ``(logp, dW, dH)`` float32.
     """
     d = hidden.shape[-1]
-    h = hidden.reshape(-1, d).astype(np.float32)
+    h = np.asarray(hidden, dtype=np.float32).reshape(-1, d)
     t = targets.reshape(-1).astype(np.int64)
     gg = g.reshape(-1).astype(np.float32)
-    e = embed.astype(np.float32)
+    e = np.asarray(embed, dtype=np.float32)
     V = e.shape[0]
     T = h.shape[0]
     tgt, mx, sm = _blocked_stats(e, h, t, softcap=softcap, vocab_chunk=vocab_chunk, sequence_chunk=sequence_chunk)
