@@ -66,6 +66,30 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
     return LIB_PATH
 
 
+XLA_FFI_SOURCE = CSRC / "lp_xla_ffi.cc"
+XLA_FFI_LIB = PKG_DIR / "liblp_b200_xla.so"
+
+
+def build_xla_ffi(force: bool = False) -> Path:
+    """Compile the XLA FFI handlers against jaxlib's headers (needs an installed ``jax``)."""
+    import jax.ffi  # noqa: PLC0415 - only where JAX exists
+
+    lib = build()
+    if not force and XLA_FFI_LIB.exists() and XLA_FFI_LIB.stat().st_mtime > max(
+        XLA_FFI_SOURCE.stat().st_mtime, lib.stat().st_mtime
+    ):
+        return XLA_FFI_LIB
+    cmd = [
+        os.environ.get("CXX", "g++"), "-std=c++17", "-O2", "-shared", "-fPIC",
+        f"-I{jax.ffi.include_dir()}", "-I/usr/local/cuda/include", str(XLA_FFI_SOURCE),
+        f"-L{PKG_DIR}", "-llp_b200", "-Wl,-rpath,$ORIGIN", "-o", str(XLA_FFI_LIB),
+    ]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"building the XLA FFI handlers failed:\n{res.stdout}\n{res.stderr}")
+    return XLA_FFI_LIB
+
+
 if __name__ == "__main__":
     flags = [a for a in sys.argv[1:] if a.startswith("-X") or a.startswith("--")]
     print(build(force=True, verbose=True, extra_flags=flags))
