@@ -659,3 +659,92 @@ int lp_scatter_rows(void* stream, const void* src, int64_t src_stride, const int
 }
 
 }  // extern "C"
+
+// ============================================================================= no-alloc forward
+// lp_fwd_noalloc: the forward of lp_fwd for callers that cannot allocate device memory at
+// the call site. Its scratch (the per-row partial max / sum of every vocabulary group and
+// the owned target logit) lives in one file-scope device array that every GPU which loads
+// this library holds until the process exits. Host code must not hand the array's name to
+// a kernel (in host code it is only a stand-in symbol): the device address is looked up
+// once per device with cudaGetSymbolAddress and cached.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(LP_NOALLOC_SCRATCH_BYTES);
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_lp_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+void* g_noalloc_scratch_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on the current device (set up on first use there).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  LP_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(LP_EINVAL, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_lp_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(LP_ECUDA, "cudaGetSymbolAddress(no-alloc scratch) on device %d: %s", dev, cudaGetErrorString(e));
+    g_noalloc_scratch_ptr[dev] = p;
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return LP_OK;
+}
+
+size_t noalloc_fwd_bytes(const GemmSched& s, int64_t T, size_t* part_bytes) {
+  *part_bytes = align_up((size_t)s.n_groups * T * sizeof(float2), 256);
+  return *part_bytes + align_up((size_t)T * 4, 256);
+}
+
+}  // namespace
+
+extern "C" int lp_fwd_noalloc(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs,
+                              int64_t v_off, const int32_t* y, float softcap, float* stats, float* logp) {
+  int rc = check_common(H, T, d, ldh, W, Vs, y);
+  if (rc) return rc;
+  if (T == 0) return LP_OK;
+  if (stats == nullptr) return fail(LP_EINVAL, "null stats");
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device_info(&di))) return rc;
+  // Same tile plan as lp_fwd, with the vocabulary groups widened until the partials fit
+  // the fixed scratch; too many tokens for even one group is refused.
+  GemmSched s = plan_fwd(T, Vs, d, di->sms);
+  size_t part_bytes = 0;
+  while (noalloc_fwd_bytes(s, T, &part_bytes) > kNoAllocScratchBytes && s.n_group < s.tiles_n) {
+    s.n_group = std::min(s.tiles_n, s.n_group * 2);
+    s.n_groups = (int)cdiv(s.tiles_n, s.n_group);
+    s.num_units = s.tiles_m * s.n_groups;
+  }
+  const size_t need = noalloc_fwd_bytes(s, T, &part_bytes);
+  if (need > kNoAllocScratchBytes)
+    return fail(LP_EINVAL,
+                "lp_fwd_noalloc: T=%lld tokens need %zu scratch bytes, above its fixed limit of %zu bytes "
+                "(LP_NOALLOC_SCRATCH_BYTES); use lp_fwd with a workspace",
+                (long long)T, need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch(&scratch))) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  float2* part = reinterpret_cast<float2*>(scratch);
+  float* tgt = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + part_bytes);
+
+  alignas(64) CUtensorMap ta, tb;
+  if ((rc = map_bf16(&ta, H, d, T, ldh, BK, BM, "hidden"))) return rc;
+  if ((rc = map_bf16(&tb, W, d, Vs, d, BK, BN, "embedding"))) return rc;
+  GemmParams p{};
+  p.s = s;
+  p.e.y = y;
+  p.e.v_off = v_off;
+  p.e.softcap = softcap;
+  p.e.part = part;
+  p.e.tgt = tgt;
+  if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di->sms, "fwd_lse_gemm")))
+    return rc;
+  ProfScope prof(st, "fwd_finalize");
+  fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, s.n_groups, (int)T, tgt, y, v_off, Vs, stats, logp);
+  LP_LAUNCH_CHECK("fwd_finalize_kernel");
+  return LP_OK;
+}

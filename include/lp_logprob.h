@@ -94,6 +94,30 @@ LP_API size_t lp_fwd_workspace_bytes(int64_t T, int64_t Vs);
 LP_API int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
            const int32_t* y, float softcap, float* stats, float* logp, void* workspace, size_t workspace_bytes);
 
+/* Size of the fixed device scratch lp_fwd_noalloc uses (held by every GPU that loads the
+ * library, from its first lp_fwd_noalloc call until the process exits). */
+#define LP_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/*
+ * Allocation-free forward. No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory where they call the logprob forward, e.g. an FFI custom
+ * call that its framework hands only input and output buffers, or a long-running host loop
+ * that must not grow device memory after start-up. It computes exactly what lp_fwd
+ * computes, with the same arguments, except that there is no workspace: the scratch is one
+ * fixed LP_NOALLOC_SCRATCH_BYTES device array inside the library.
+ *   - Nothing is allocated: no cudaMalloc / cudaFree, no allocating library call.
+ *   - The first call on a device looks up that device's scratch address (the device must
+ *     be current); make that first call before any stream capture.
+ *   - All calls share the one array, so calls that overlap on the GPU (different streams,
+ *     or different host threads) race and corrupt each other's results: serialise them.
+ *     The array keeps the last call's contents; every scratch value a call reads is
+ *     written earlier in that same call, so nothing needs clearing between calls.
+ *   - Token counts whose scratch exceeds the limit (about 690k tokens; fewer when the
+ *     tile plan keeps several vocabulary groups) return LP_EINVAL with a message.
+ */
+LP_API int lp_fwd_noalloc(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs,
+                          int64_t v_off, const int32_t* y, float softcap, float* stats, float* logp);
+
 /*
  * Merge P per-shard triples (replaces the pmax / psum combine of losses.py:219,243-245).
  *   shard_stats f32 [P, 3, T] (lp_fwd's `stats` of every shard, in shard order)
