@@ -1,0 +1,81 @@
+"""One rank of the multi-GPU parity check (launched by tests/test_gpu_multirank.py via torchrun).
+
+Every rank draws the same seeded inputs, keeps its vocabulary row block, and runs the
+public API (per_token_logps and completion_logps, forward + backward) over an NCCL mesh.
+Rank 0 gathers the dW shards and checks logps, dH and dW against the CPU oracle.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from gemma4_posttrain_jax_b200 import completion_logps, make_mesh, per_token_logps, shard_rows  # noqa: E402
+from oracle import logprob_oracle as orc  # noqa: E402
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def main() -> int:
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    mesh = make_mesh()
+    rng = np.random.default_rng(20260925)
+    V, T, d = 1024 * world + 0, 777, 160
+    w = orc.bf16_round(rng.normal(size=(V, d)) * 1.5)
+    h = orc.bf16_round(rng.normal(size=(T, d)))
+    y = rng.integers(0, V, size=T).astype(np.int32)
+    y[:4] = [0, V // world - 1, V // world, V - 1]
+    g = rng.normal(size=T).astype(np.float32)
+    W = shard_rows(torch.from_numpy(w), mesh).to(dev).to(torch.bfloat16).requires_grad_(True)
+    H = torch.from_numpy(h).to(dev).to(torch.bfloat16).requires_grad_(True)
+    lp = per_token_logps(W, H, torch.from_numpy(y).to(dev), softcap=30.0, mesh=mesh)
+    (lp * torch.from_numpy(g).to(dev)).sum().backward()
+    dW_parts = [torch.empty_like(W.grad) for _ in range(world)]
+    dist.all_gather(dW_parts, W.grad)
+    ok = True
+    if rank == 0:
+        lp_ref, dW_ref, dH_ref = orc.logps_grads_f64(w, h, y, g, 30.0)
+        e_lp = float(np.abs(lp.detach().cpu().numpy() - lp_ref).max())
+        e_h = rel_l2(H.grad.float().cpu().numpy(), dH_ref)
+        e_w = rel_l2(torch.cat(dW_parts).float().cpu().numpy(), dW_ref)
+        print(f"world={world}: logp max abs {e_lp:.2e}, dH rel-L2 {e_h:.2e}, dW rel-L2 {e_w:.2e}", flush=True)
+        ok = e_lp <= 2e-3 and e_h <= 1e-2 and e_w <= 1e-2
+    # GRPO caller, response slots compacted, same mesh
+    B, Pw, N = 3, 5, 40
+    hid = orc.bf16_round(rng.normal(size=(B, Pw + N, d)))
+    ids = rng.integers(0, V, size=(B, N)).astype(np.int32)
+    mask = np.arange(N)[None, :] < np.array([40, 7, 0])[:, None]
+    Hd = torch.from_numpy(hid).to(dev).to(torch.bfloat16).requires_grad_(True)
+    out = completion_logps(W.detach(), Hd, torch.from_numpy(ids).to(dev), torch.from_numpy(mask).to(dev),
+                           prompt_width=Pw, softcap=30.0, mesh=mesh)
+    out.sum().backward()
+    if rank == 0:
+        resp = hid[:, Pw - 1: Pw - 1 + N]
+        ref = orc.dense_logps(w, resp, np.where(mask, ids, 0), 30.0)
+        got = out.detach().cpu().numpy()
+        e2 = float(np.abs(got[mask] - ref[mask]).max())
+        print(f"world={world}: completion logp max abs {e2:.2e}, invalid slots zero: {(got[~mask] == 0).all()}",
+              flush=True)
+        ok = ok and e2 <= 2e-3 and bool((got[~mask] == 0).all())
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.broadcast(flag, 0)
+    dist.destroy_process_group()
+    return 0 if int(flag.item()) == 1 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,80 @@
+"""Host-side behaviour of the Python mirror, no GPU needed: argument validation (same
+messages as the reference), no silent fallback, checkpoint identity (mirrors
+``tests/test_logprob_backends.py`` of the reference)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from gemma4_posttrain_jax_b200 import logprob_protocol as proto
+from gemma4_posttrain_jax_b200 import ops
+from gemma4_posttrain_jax_b200.losses import completion_logps, per_token_logps, sft_token_logps
+
+
+def test_shape_mismatch_message_matches_reference():
+    with pytest.raises(ValueError, match="does not match"):
+        per_token_logps(torch.ones((7, 3)), torch.ones((2, 4, 3)), torch.ones((2, 3), dtype=torch.int32), softcap=None)
+
+
+def test_incompatible_embedding_and_chunk_checks():
+    with pytest.raises(ValueError, match="incompatible embedding"):
+        per_token_logps(torch.ones((7, 3)), torch.ones((2, 4)), torch.ones((2,), dtype=torch.int32), softcap=None)
+    with pytest.raises(ValueError, match="must be positive"):
+        per_token_logps(torch.ones((7, 3)), torch.ones((2, 3)), torch.ones((2,), dtype=torch.int32), softcap=None,
+                        vocab_chunk=0)
+    with pytest.raises(ValueError, match="softcap must be finite"):
+        per_token_logps(torch.ones((7, 3)), torch.ones((2, 3)), torch.ones((2,), dtype=torch.int32), softcap=-1.0)
+
+
+@pytest.mark.parametrize("backend,message", [("unknown", "unknown logprob"), ("jax", "backend='cuda'"),
+                                             ("pallas", "backend='cuda'")])
+def test_invalid_backend_never_silently_falls_back(backend, message):
+    w = torch.ones((8, 8), dtype=torch.bfloat16)
+    h = torch.ones((2, 8), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match=message):
+        per_token_logps(w, h, torch.zeros((2,), dtype=torch.int32), softcap=30.0, backend=backend)
+
+
+def test_cpu_tensors_are_refused_not_computed():
+    w = torch.ones((8, 8), dtype=torch.bfloat16)
+    h = torch.ones((2, 8), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="no CPU fallback"):
+        per_token_logps(w, h, torch.zeros((2,), dtype=torch.int32), softcap=30.0)
+    with pytest.raises(ValueError, match="no CPU fallback"):
+        ops.shard_forward(w, h, torch.zeros((2,), dtype=torch.int32), None)
+    with pytest.raises(ValueError, match="no CPU fallback"):
+        ops.compact(torch.ones((2, 3), dtype=torch.bool))
+
+
+def test_caller_shape_checks():
+    with pytest.raises(ValueError, match="prompt_width"):
+        completion_logps(torch.ones((8, 8)), torch.ones((2, 4, 8)), torch.zeros((2, 4), dtype=torch.int32),
+                         torch.ones((2, 4), dtype=torch.bool), prompt_width=2, softcap=None)
+    with pytest.raises(ValueError, match="at least two tokens"):
+        sft_token_logps(torch.ones((8, 8)), torch.ones((2, 1, 8)), torch.zeros((2, 1), dtype=torch.int64), softcap=None)
+
+
+def test_legacy_checkpoint_keeps_native_backend():
+    saved = {"mode": "gsm8k", "seed": 7}
+    proto.validate_logprob_resume(saved, {**saved, "logprob_backend": "jax"})
+    with pytest.raises(ValueError, match="logprob_backend"):
+        proto.validate_logprob_resume(saved, {**saved, **proto.logprob_run_metadata("cuda")})
+
+
+def test_cuda_checkpoint_identity_and_changes_refused():
+    meta = proto.logprob_run_metadata("cuda")
+    assert meta == {"logprob_backend": "cuda", "logprob_protocol": proto.CUDA_LOGPROB_PROTOCOL}
+    saved = {"mode": "overfit", **meta}
+    proto.validate_logprob_resume(saved, dict(saved))
+    with pytest.raises(ValueError, match="logprob_backend"):
+        proto.validate_logprob_resume(saved, {**saved, **proto.logprob_run_metadata("pallas")})
+    with pytest.raises(ValueError, match="logprob_protocol"):
+        proto.validate_logprob_resume({**saved, "logprob_protocol": "older"}, saved)
+
+
+def test_native_metadata_is_empty_and_unknown_rejected():
+    assert proto.logprob_run_metadata("jax") == {}
+    assert proto.logprob_run_metadata("pallas")["logprob_protocol"] == proto.PALLAS_LOGPROB_PROTOCOL
+    with pytest.raises(ValueError, match="unknown logprob"):
+        proto.logprob_run_metadata("unknown")
