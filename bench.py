@@ -53,6 +53,8 @@ def parse_args():
     p.add_argument("--softcap", type=float, default=SOFTCAP, help="<= 0 disables the softcap")
     p.add_argument("--batch", type=int, default=B, help="sequences (default: config 2's 128)")
     p.add_argument("--token-chunk", type=int, default=0, help="backward token chunk (0 = library default)")
+    p.add_argument("--cta-group", type=int, default=0, choices=(0, 1, 2),
+                   help="tensor-core CTA group of the GEMMs (0 = library default, the CTA pair)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
@@ -97,6 +99,12 @@ def config_dict(batch, n_valid, world, softcap):
         "parallelism": f"vocab{world}",
         "l2": "no flush: W shard + hidden exceed the 126 MB L2 (>= 0.8 GB each)",
     }
+
+
+def cta_group_of_run():
+    from gemma4_posttrain_jax_b200 import _lib
+
+    return _lib.cta_group()
 
 
 # --------------------------------------------------------------------------- clocks
@@ -261,6 +269,8 @@ def main():
     if not _lib.LIB_PATH.exists():
         build.build()
     _lib.load()
+    if args.cta_group:
+        _lib.set_cta_group(args.cta_group)
     mesh = None
     if world > 1:
         from datetime import timedelta
@@ -440,6 +450,7 @@ def main():
             "step_tflops": step_tflops,
             "step_frac_of_sustained_peak": step_tflops / world / peaks["bf16_tflops_sustained"],
             "kernels": kernels,
+            "cta_group": cta_group_of_run(),
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -33,6 +33,9 @@ _SIG = {
     "lp_last_error": (ctypes.c_char_p, []),
     "lp_launch_count": (ctypes.c_longlong, []),
     "lp_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "lp_set_cta_group": (ctypes.c_int, [ctypes.c_int]),
+    "lp_get_cta_group": (ctypes.c_int, []),
+    "lp_device_pairs": (ctypes.c_int, []),
     "lp_profile_enable": (ctypes.c_int, [ctypes.c_int]),
     "lp_profile_read": (
         ctypes.c_int,
@@ -126,6 +129,15 @@ def profile_read(max_tags: int = 32) -> dict[str, tuple[float, int]]:
         name = raw[32 * k : 32 * k + 32].split(b"\0", 1)[0].decode()
         out[name] = (float(ms[k]), int(cnt[k]))
     return out
+
+
+def set_cta_group(cg: int) -> None:
+    """Select the pair (2, default) or single-CTA (1) tensor-core GEMMs for later calls."""
+    check(load().lp_set_cta_group(int(cg)), "lp_set_cta_group")
+
+
+def cta_group() -> int:
+    return int(load().lp_get_cta_group())
 
 
 def launch_count() -> int:

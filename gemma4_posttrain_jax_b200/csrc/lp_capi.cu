@@ -6,6 +6,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -89,13 +90,55 @@ int fail(int code, const char* fmt, ...) {
 
 constexpr int kMaxDevices = 64;
 
+// Tensor-core CTA group of the GEMMs: 2 = CTA pairs with 256x256 tiles (default), 1 = single
+// CTAs with 128x256 tiles. LP_B200_CTA_GROUP=1 in the environment or lp_set_cta_group()
+// selects the single-CTA kernels (kept as the reference point of the pair kernels).
+std::atomic<int> g_cg{0};
+
+int cta_group() {
+  int v = g_cg.load();
+  if (v == 0) {
+    const char* e = getenv("LP_B200_CTA_GROUP");
+    v = (e != nullptr && e[0] == '1') ? 1 : 2;
+    g_cg.store(v);
+  }
+  return v;
+}
+
 struct DeviceInfo {
   int sms = 0;
   int major = 0, minor = 0;
+  int pairs = 0;  // CTA pairs of the pair GEMMs that can be resident at once
   bool ready = false;
 };
+
+// Persistent workers of a launch: SMs for CG = 1, co-resident CTA pairs for CG = 2.
+int workers(const DeviceInfo* di, int cg) { return cg == 1 ? di->sms : di->pairs; }
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
+
+// How many 2-CTA clusters of the largest pair GEMM (most shared memory) fit on the GPU at
+// once; the persistent pair kernels launch at most this many pairs.
+int max_resident_pairs(int sms, int* pairs) {
+  auto kern = tc_gemm_kernel<2, EPI_BWD_DZ, false, false, true>;
+  constexpr int smem = gemm_smem_bytes<2, EPI_BWD_DZ>();
+  LP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  LP_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+  *pairs = std::max(1, std::min(n, sms / 2));
+  return LP_OK;
+}
 
 int current_device_info(DeviceInfo** out) {
   int dev = 0;
@@ -107,6 +150,11 @@ int current_device_info(DeviceInfo** out) {
     LP_CUDA_TRY(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
     LP_CUDA_TRY(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev));
     LP_CUDA_TRY(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev));
+    d.pairs = d.sms / 2;
+    if (d.major == 10 && d.minor == 0) {
+      int rc = max_resident_pairs(d.sms, &d.pairs);
+      if (rc) return rc;
+    }
     d.ready = true;
   }
   if (d.major != 10 || d.minor != 0)
@@ -166,12 +214,13 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Forward: N tiles grouped G per unit; pick the largest G within 1% of the best critical
 // path (units are dealt round-robin to `sms` persistent CTAs).
-GemmSched plan_fwd(int64_t T, int64_t Vs, int64_t d, int sms) {
+GemmSched plan_fwd(int64_t T, int64_t Vs, int64_t d, int sms, int bm) {
   GemmSched s{};
+  s.bm = bm;
   s.M = (int)T;
   s.N = (int)Vs;
   s.K = (int)d;
-  s.tiles_m = (int)cdiv(T, BM);
+  s.tiles_m = (int)cdiv(T, bm);
   s.tiles_n = (int)cdiv(Vs, BN);
   s.k_blocks = (int)cdiv(d, BK);
   s.k_splits = 1;
@@ -196,12 +245,13 @@ GemmSched plan_fwd(int64_t T, int64_t Vs, int64_t d, int sms) {
 
 // Plain GEMM with optional split-K: pick S in [1, 16] minimising the critical path,
 // keeping at least 8 K blocks per split; ties prefer fewer splits.
-GemmSched plan_gemm(int64_t M, int64_t N, int64_t K, int sms, bool allow_split, int n_fast) {
+GemmSched plan_gemm(int64_t M, int64_t N, int64_t K, int sms, bool allow_split, int n_fast, int bm) {
   GemmSched s{};
+  s.bm = bm;
   s.M = (int)M;
   s.N = (int)N;
   s.K = (int)K;
-  s.tiles_m = (int)cdiv(M, BM);
+  s.tiles_m = (int)cdiv(M, bm);
   s.tiles_n = (int)cdiv(N, BN);
   s.k_blocks = (int)cdiv(K, BK);
   s.n_group = 1;
@@ -232,7 +282,7 @@ int64_t default_token_chunk(int64_t T, int64_t Vs) {
   const int64_t ldz = (Vs + 7) / 8 * 8;
   const int64_t budget = int64_t(4) << 30;  // bytes of bf16 dZ per chunk
   int64_t tc = budget / (ldz * 2);
-  tc = std::max<int64_t>(BM, tc / BM * BM);
+  tc = std::max<int64_t>(256, tc / 256 * 256);
   return std::min<int64_t>(tc, std::max<int64_t>(T, 1));
 }
 
@@ -243,20 +293,20 @@ struct BwdLayout {
   int64_t mpad;
 };
 
-BwdLayout bwd_layout(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int flags, int sms) {
+BwdLayout bwd_layout(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int flags, int sms, int bm) {
   BwdLayout L{};
   L.tc = token_chunk > 0 ? std::min<int64_t>(token_chunk, std::max<int64_t>(T, 1)) : default_token_chunk(T, Vs);
   L.chunks = T > 0 ? cdiv(T, L.tc) : 0;
   L.ldz = (Vs + 7) / 8 * 8;
-  L.mpad = cdiv(L.tc, BM) * BM;
+  L.mpad = cdiv(L.tc, bm) * bm;
   // the largest split-K of any chunk (the first chunk is the largest)
   L.max_splits = 1;
   if (!(flags & LP_BWD_NO_DH) && T > 0) {
-    GemmSched s = plan_gemm(L.tc, d, Vs, sms, true, 1);
+    GemmSched s = plan_gemm(L.tc, d, Vs, sms, true, 1, bm);
     L.max_splits = s.k_splits;
     // a shorter last chunk may choose more splits
     const int64_t last = T - (L.chunks - 1) * L.tc;
-    GemmSched s2 = plan_gemm(last, d, Vs, sms, true, 1);
+    GemmSched s2 = plan_gemm(last, d, Vs, sms, true, 1, bm);
     L.max_splits = std::max(L.max_splits, s2.k_splits);
   }
   size_t off = 0;
@@ -271,31 +321,58 @@ BwdLayout bwd_layout(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int 
 }
 
 // --------------------------------------------------------------------------- launches
-template <int EPI, bool A_MN, bool B_MN, bool CAP>
-int launch_gemm(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
-                const GemmParams& p, int sms, const char* tag) {
-  auto kern = tc_gemm_kernel<EPI, A_MN, B_MN, CAP>;
-  constexpr int smem = gemm_smem_bytes<EPI>();
+template <int CG, int EPI, bool A_MN, bool B_MN, bool CAP>
+int launch_gemm_cg(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
+                   const GemmParams& p, const DeviceInfo* di, const char* tag) {
+  auto kern = tc_gemm_kernel<CG, EPI, A_MN, B_MN, CAP>;
+  constexpr int smem = gemm_smem_bytes<CG, EPI>();
   static bool configured[kMaxDevices] = {};
   int dev = 0;
   LP_CUDA_TRY(cudaGetDevice(&dev));
   if (!configured[dev]) {
     LP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if (CG == 2) LP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
     configured[dev] = true;
   }
-  const int grid = std::max(1, std::min(p.s.num_units, sms));
+  const int grid = CG * std::max(1, std::min(p.s.num_units, workers(di, CG)));
   ProfScope prof(st, tag);
-  kern<<<grid, NUM_THREADS, smem, st>>>(a, b, o, p);
+  if constexpr (CG == 1) {
+    kern<<<grid, NUM_THREADS, smem, st>>>(a, b, o, p);
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    LP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, b, o, p));
+  }
   LP_LAUNCH_CHECK("tc_gemm_kernel");
   return LP_OK;
 }
 
+template <int EPI, bool A_MN, bool B_MN, bool CAP>
+int launch_gemm(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
+                const GemmParams& p, const DeviceInfo* di, const char* tag) {
+  return p.s.bm == 256 ? launch_gemm_cg<2, EPI, A_MN, B_MN, CAP>(st, a, b, o, p, di, tag)
+                       : launch_gemm_cg<1, EPI, A_MN, B_MN, CAP>(st, a, b, o, p, di, tag);
+}
+
 template <int EPI, bool A_MN, bool B_MN>
 int launch_gemm_cap(bool cap, cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
-                    const GemmParams& p, int sms, const char* tag) {
-  return cap ? launch_gemm<EPI, A_MN, B_MN, true>(st, a, b, o, p, sms, tag)
-             : launch_gemm<EPI, A_MN, B_MN, false>(st, a, b, o, p, sms, tag);
+                    const GemmParams& p, const DeviceInfo* di, const char* tag) {
+  return cap ? launch_gemm<EPI, A_MN, B_MN, true>(st, a, b, o, p, di, tag)
+             : launch_gemm<EPI, A_MN, B_MN, false>(st, a, b, o, p, di, tag);
 }
+
+// Box height of a K-major B operand: the rows of B one CTA stages.
+uint32_t b_box_rows(int cg) { return (uint32_t)(BN / cg); }
 
 int check_common(const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, const int32_t* y) {
   if (T < 0 || d <= 0 || Vs <= 0) return fail(LP_EINVAL, "bad sizes T=%lld d=%lld Vs=%lld", (long long)T, (long long)d,
@@ -318,6 +395,19 @@ int lp_version(void) { return 100; }
 const char* lp_last_error(void) { return g_last_error.c_str(); }
 
 long long lp_launch_count(void) { return g_launches.load(); }
+
+int lp_device_pairs(void) {
+  DeviceInfo* di = nullptr;
+  return current_device_info(&di) == LP_OK ? di->pairs : -1;
+}
+
+int lp_set_cta_group(int cg) {
+  if (cg != 1 && cg != 2) return fail(LP_EINVAL, "cta group must be 1 or 2, got %d", cg);
+  g_cg.store(cg);
+  return LP_OK;
+}
+
+int lp_get_cta_group(void) { return cta_group(); }
 
 int lp_profile_enable(int on) {
   std::lock_guard<std::mutex> lk(g_prof_mu);
@@ -378,7 +468,8 @@ size_t lp_fwd_workspace_bytes(int64_t T, int64_t Vs) {
   int sms = 148;
   if (current_device_info(&di) == LP_OK) sms = di->sms;
   if (T <= 0 || Vs <= 0) return 256;
-  GemmSched s = plan_fwd(T, Vs, 64, sms);
+  const int cg = cta_group();
+  GemmSched s = plan_fwd(T, Vs, 64, di != nullptr ? workers(di, cg) : (cg == 1 ? sms : sms / 2), 128 * cg);
   return align_up((size_t)s.n_groups * T * sizeof(float2), 256) + align_up((size_t)T * 4, 256);
 }
 
@@ -391,7 +482,8 @@ int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
   DeviceInfo* di = nullptr;
   if ((rc = current_device_info(&di))) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  GemmSched s = plan_fwd(T, Vs, d, di->sms);
+  const int cg = cta_group();
+  GemmSched s = plan_fwd(T, Vs, d, workers(di, cg), 128 * cg);
   const size_t part_bytes = align_up((size_t)s.n_groups * T * sizeof(float2), 256);
   const size_t need = part_bytes + align_up((size_t)T * 4, 256);
   if (workspace == nullptr || workspace_bytes < need)
@@ -400,8 +492,8 @@ int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
   float* tgt = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + part_bytes);
 
   alignas(64) CUtensorMap ta, tb;
-  if ((rc = map_bf16(&ta, H, d, T, ldh, BK, BM, "hidden"))) return rc;
-  if ((rc = map_bf16(&tb, W, d, Vs, d, BK, BN, "embedding"))) return rc;
+  if ((rc = map_bf16(&ta, H, d, T, ldh, BK, 128, "hidden"))) return rc;
+  if ((rc = map_bf16(&tb, W, d, Vs, d, BK, b_box_rows(cg), "embedding"))) return rc;
   GemmParams p{};
   p.s = s;
   p.e.y = y;
@@ -409,8 +501,7 @@ int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
   p.e.softcap = softcap;
   p.e.part = part;
   p.e.tgt = tgt;
-  if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di->sms, "fwd_lse_gemm")))
-    return rc;
+  if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di, "fwd_lse_gemm"))) return rc;
   ProfScope prof(st, "fwd_finalize");
   fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, s.n_groups, (int)T, tgt, y, v_off, Vs, stats, logp);
   LP_LAUNCH_CHECK("fwd_finalize_kernel");
@@ -433,7 +524,10 @@ size_t lp_bwd_workspace_bytes(int64_t T, int64_t d, int64_t Vs, int64_t token_ch
   int sms = 148;
   if (current_device_info(&di) == LP_OK) sms = di->sms;
   if (T <= 0 || Vs <= 0 || d <= 0) return 256;
-  return bwd_layout(T, d, Vs, token_chunk, flags, sms).total + 256;
+  const int cg = cta_group();
+  return bwd_layout(T, d, Vs, token_chunk, flags, di != nullptr ? workers(di, cg) : (cg == 1 ? sms : sms / 2),
+                    128 * cg).total +
+         256;
 }
 
 int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
@@ -455,7 +549,9 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
     if (want_dw) LP_CUDA_TRY(cudaMemsetAsync(dW, 0, (size_t)Vs * d * (dw_bf16 ? 2 : 4), st));
     return LP_OK;
   }
-  const BwdLayout L = bwd_layout(T, d, Vs, token_chunk, flags, di->sms);
+  const int cg = cta_group();
+  const int bm = 128 * cg, nw = workers(di, cg);
+  const BwdLayout L = bwd_layout(T, d, Vs, token_chunk, flags, nw, bm);
   if (workspace == nullptr || workspace_bytes < L.total)
     return fail(LP_EWORKSPACE, "lp_bwd needs %zu workspace bytes, got %zu", L.total, workspace_bytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & 1023) != 0) return fail(LP_EINVAL, "workspace must be 1024-byte aligned");
@@ -475,26 +571,26 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
     // 1) recompute logits tile by tile and write dZ (bf16) for this chunk
     {
       alignas(64) CUtensorMap ta, tb, to;
-      if ((rc = map_bf16(&ta, Hc, d, tcur, ldh, BK, BM, "hidden chunk"))) return rc;
-      if ((rc = map_bf16(&tb, W, d, Vs, d, BK, BN, "embedding"))) return rc;
+      if ((rc = map_bf16(&ta, Hc, d, tcur, ldh, BK, 128, "hidden chunk"))) return rc;
+      if ((rc = map_bf16(&tb, W, d, Vs, d, BK, b_box_rows(cg), "embedding"))) return rc;
       if ((rc = map_bf16(&to, dz, Vs, tcur, L.ldz, 64, 32, "dZ store"))) return rc;
       GemmParams p{};
-      p.s = plan_gemm(tcur, Vs, d, di->sms, false, 0);
+      p.s = plan_gemm(tcur, Vs, d, nw, false, 0, bm);
       p.e.y = y + t0;
       p.e.v_off = v_off;
       p.e.softcap = softcap;
       p.e.g = g + t0;
       p.e.stats = norm + t0;
       p.e.stats_ld = T;
-      if ((rc = launch_gemm_cap<EPI_BWD_DZ, false, false>(cap, st, ta, tb, to, p, di->sms, "bwd_dz_gemm"))) return rc;
+      if ((rc = launch_gemm_cap<EPI_BWD_DZ, false, false>(cap, st, ta, tb, to, p, di, "bwd_dz_gemm"))) return rc;
     }
     // 2) dH[t0:t0+tcur] = dZ . W
     if (want_dh) {
       alignas(64) CUtensorMap ta, tb, to;
-      if ((rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, BK, BM, "dZ as A"))) return rc;
+      if ((rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, BK, 128, "dZ as A"))) return rc;
       if ((rc = map_bf16(&tb, W, d, Vs, d, 64, 64, "embedding as MN-major B"))) return rc;
       GemmParams p{};
-      p.s = plan_gemm(tcur, d, Vs, di->sms, true, 1);
+      p.s = plan_gemm(tcur, d, Vs, nw, true, 1, bm);
       char* dh_c = reinterpret_cast<char*>(dH) + (size_t)t0 * ld_dh * (dh_f32 ? 4 : 2);
       if (p.s.k_splits == 1) {
         if (dh_f32) {
@@ -510,7 +606,7 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
         p.e.store_mode = STORE_F32;
         p.e.split_rows = (int)L.mpad;
       }
-      if ((rc = launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di->sms, "bwd_dh_gemm"))) return rc;
+      if ((rc = launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di, "bwd_dh_gemm"))) return rc;
       if (p.s.k_splits > 1) {
         const int64_t total = tcur * (d / 4);
         const unsigned grid = (unsigned)std::min<int64_t>(cdiv(total, 256), (int64_t)di->sms * 8);
@@ -525,7 +621,7 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
       if ((rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, 64, 64, "dZ as MN-major A"))) return rc;
       if ((rc = map_bf16(&tb, Hc, d, tcur, ldh, 64, 64, "hidden as MN-major B"))) return rc;
       GemmParams p{};
-      p.s = plan_gemm(Vs, d, tcur, di->sms, false, 1);
+      p.s = plan_gemm(Vs, d, tcur, nw, false, 1, bm);
       const bool direct_bf16 = dw_bf16 && L.chunks == 1;
       if (direct_bf16) {
         if ((rc = map_bf16(&to, dW, d, Vs, d, 64, 32, "dW store"))) return rc;
@@ -534,7 +630,7 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
         if ((rc = map_f32(&to, dw_acc, d, Vs, d, 32, 32, "dW store"))) return rc;
         p.e.store_mode = c == 0 ? STORE_F32 : STORE_F32_ADD;
       }
-      if ((rc = launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di->sms, "bwd_dw_gemm"))) return rc;
+      if ((rc = launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di, "bwd_dw_gemm"))) return rc;
     }
   }
   if (want_dw && dw_bf16 && L.chunks > 1) {
@@ -560,19 +656,20 @@ int lp_gemm_bf16(void* stream, const void* A, int64_t M, int64_t K, int64_t lda,
   alignas(64) CUtensorMap ta, tb, to;
   // K-major A: [M rows][K], MN-major A: [K rows][M]; likewise B with N.
   if (a_mn) rc = map_bf16(&ta, A, M, K, lda, 64, 64, "A (MN-major)");
-  else rc = map_bf16(&ta, A, K, M, lda, BK, BM, "A (K-major)");
+  else rc = map_bf16(&ta, A, K, M, lda, BK, 128, "A (K-major)");
   if (rc) return rc;
+  const int cg = cta_group();
   if (b_mn) rc = map_bf16(&tb, B, N, K, ldb, 64, 64, "B (MN-major)");
-  else rc = map_bf16(&tb, B, K, N, ldb, BK, BN, "B (K-major)");
+  else rc = map_bf16(&tb, B, K, N, ldb, BK, b_box_rows(cg), "B (K-major)");
   if (rc) return rc;
   if ((rc = map_f32(&to, D, N, M, ldd, 32, 32, "D"))) return rc;
   GemmParams p{};
-  p.s = plan_gemm(M, N, K, di->sms, false, 0);
+  p.s = plan_gemm(M, N, K, workers(di, cg), false, 0, 128 * cg);
   p.e.store_mode = STORE_F32;
-  if (!a_mn && !b_mn) return launch_gemm<EPI_STORE, false, false, false>(st, ta, tb, to, p, di->sms, "gemm");
-  if (!a_mn && b_mn) return launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di->sms, "gemm");
-  if (a_mn && b_mn) return launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di->sms, "gemm");
-  return launch_gemm<EPI_STORE, true, false, false>(st, ta, tb, to, p, di->sms, "gemm");
+  if (!a_mn && !b_mn) return launch_gemm<EPI_STORE, false, false, false>(st, ta, tb, to, p, di, "gemm");
+  if (!a_mn && b_mn) return launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di, "gemm");
+  if (a_mn && b_mn) return launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di, "gemm");
+  return launch_gemm<EPI_STORE, true, false, false>(st, ta, tb, to, p, di, "gemm");
 }
 
 size_t lp_compact_workspace_bytes(int64_t B, int64_t N) {
@@ -712,7 +809,8 @@ extern "C" int lp_fwd_noalloc(void* stream, const void* H, int64_t T, int64_t d,
   if ((rc = current_device_info(&di))) return rc;
   // Same tile plan as lp_fwd, with the vocabulary groups widened until the partials fit
   // the fixed scratch; too many tokens for even one group is refused.
-  GemmSched s = plan_fwd(T, Vs, d, di->sms);
+  const int cg = cta_group();
+  GemmSched s = plan_fwd(T, Vs, d, workers(di, cg), 128 * cg);
   size_t part_bytes = 0;
   while (noalloc_fwd_bytes(s, T, &part_bytes) > kNoAllocScratchBytes && s.n_group < s.tiles_n) {
     s.n_group = std::min(s.tiles_n, s.n_group * 2);
@@ -732,8 +830,8 @@ extern "C" int lp_fwd_noalloc(void* stream, const void* H, int64_t T, int64_t d,
   float* tgt = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + part_bytes);
 
   alignas(64) CUtensorMap ta, tb;
-  if ((rc = map_bf16(&ta, H, d, T, ldh, BK, BM, "hidden"))) return rc;
-  if ((rc = map_bf16(&tb, W, d, Vs, d, BK, BN, "embedding"))) return rc;
+  if ((rc = map_bf16(&ta, H, d, T, ldh, BK, 128, "hidden"))) return rc;
+  if ((rc = map_bf16(&tb, W, d, Vs, d, BK, b_box_rows(cg), "embedding"))) return rc;
   GemmParams p{};
   p.s = s;
   p.e.y = y;
@@ -741,8 +839,7 @@ extern "C" int lp_fwd_noalloc(void* stream, const void* H, int64_t T, int64_t d,
   p.e.softcap = softcap;
   p.e.part = part;
   p.e.tgt = tgt;
-  if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di->sms, "fwd_lse_gemm")))
-    return rc;
+  if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di, "fwd_lse_gemm"))) return rc;
   ProfScope prof(st, "fwd_finalize");
   fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, s.n_groups, (int)T, tgt, y, v_off, Vs, stats, logp);
   LP_LAUNCH_CHECK("fwd_finalize_kernel");

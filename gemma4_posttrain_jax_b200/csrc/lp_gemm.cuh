@@ -2,18 +2,24 @@
 //
 //   D[M, N] = A[M, K] . B[N, K]^T       (bf16 operands, f32 accumulation in TMEM)
 //
-// One CTA per SM walks a static round-robin list of work units. A unit is one 128-row
-// M tile, a run of consecutive 256-column N tiles and a range of 64-deep K blocks.
+// CG = 1: one CTA per SM computes 128x256 tiles (tcgen05.mma.cta_group::1, M=128 N=256).
+// CG = 2: a cluster of two CTAs on two SMs computes 256x256 tiles with one
+//         tcgen05.mma.cta_group::2 (M=256 N=256) issued by the pair leader. Each CTA stages
+//         its own 128 rows of A and its own half (128 rows) of B, so per SM the operand
+//         traffic per MMA-FLOP drops by a third and the smem ring gets 6 stages instead of 4.
+//         Each CTA's TMEM holds the accumulator rows of its half of the M tile.
 //
-//   warp 0      : TMA producer (one thread) -> NUM_STAGES-deep smem ring (48 KB / stage)
-//   warp 1      : TMEM allocator + MMA issuer (one thread), tcgen05.mma M=128 N=256 K=16
+// Persistent CTAs (CG = 2: CTA pairs) walk a static round-robin list of work units. A unit
+// is one M tile (128*CG rows), a run of consecutive 256-column N tiles and a range of
+// 64-deep K blocks.
+//
+//   warp 0      : TMA producer (one thread)  -> NUM_STAGES-deep smem ring
+//   warp 1      : TMEM allocator + MMA issuer (one thread; in the pair leader only)
 //   warps 2..5  : epilogue; warp w reads TMEM lanes 32*(w%4).. (its 32 rows of the tile)
 //
-// The two 128x256 f32 accumulators (512 TMEM columns) are double-buffered, so the
-// epilogue of tile i overlaps the MMAs of tile i+1.
-//
-// Operands are either K-major (rows of the tile contiguous along K) or MN-major
-// (contiguous along M / N); both are staged by TMA with 128-byte swizzle.
+// The two 256-column f32 accumulators (512 TMEM columns) are double-buffered, so the
+// epilogue of tile i overlaps the MMAs of tile i+1. Operands are K-major or MN-major,
+// staged by TMA with 128-byte swizzle.
 //
 // Epilogues:
 //   EPI_FWD_LSE : softcap + running (max, sum-exp) per row in base 2 + target pick, never
@@ -21,29 +27,40 @@
 //   EPI_BWD_DZ  : recompute path; dZ = g * (onehot - softmax) * softcap' written as bf16
 //                 through swizzled smem staging + TMA store.
 //   EPI_STORE   : plain f32 / bf16 store or f32 TMA reduce-add of the accumulator.
+//
+// Synchronisation (all waits bounded, see lp_ptx.cuh):
+//   full[s]   : TMA -> MMA. CG=2: lives in the leader, counts both CTAs' bytes.
+//   empty[s]  : MMA -> TMA, in every CTA; the MMA thread commits to each CTA's copy.
+//   tfull[b]  : MMA -> epilogue, in every CTA (commit per CTA).
+//   tempty[b] : epilogue -> MMA, in the leader; every epilogue warp of the pair arrives.
 #pragma once
 
 #include "lp_ptx.cuh"
 
 namespace lpk {
 
-constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
-constexpr int NUM_STAGES = 4;
 constexpr int EPI_WARPS = 4;
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int STAGING_BUF_BYTES = 32 * 128;                 // 32 rows x 128 B, one TMA box
+constexpr int A_STAGE_BYTES = 128 * BK * 2;                // 16 KB: 128 rows of A per CTA
+constexpr int STAGING_BUF_BYTES = 32 * 128;                // 32 rows x 128 B, one TMA box
 constexpr int STAGING_WARP_BYTES = 2 * STAGING_BUF_BYTES;  // double-buffered per warp
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 enum : int { EPI_FWD_LSE = 0, EPI_BWD_DZ = 1, EPI_STORE = 2 };
 enum : int { STORE_BF16 = 0, STORE_F32 = 1, STORE_F32_ADD = 2 };
+
+template <int CG>
+struct Cfg {
+  static constexpr int BM = 128 * CG;                      // rows of one M tile (the pair's for CG=2)
+  static constexpr int B_ROWS = BN / CG;                   // rows of B staged by each CTA
+  static constexpr int B_STAGE_BYTES = B_ROWS * BK * 2;    // 32 KB (CG=1) / 16 KB (CG=2)
+  static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+  static constexpr int NUM_STAGES = CG == 1 ? 4 : 6;
+};
 
 struct GemmSched {
   int M, N, K;
@@ -52,6 +69,7 @@ struct GemmSched {
   int k_splits, kb_per_split;
   int num_units;
   int n_fast;  // 1: consecutive units step through N groups first (share the A tile)
+  int bm;      // rows per M tile (128 * CG)
 };
 
 struct EpiParams {
@@ -107,45 +125,51 @@ __host__ __device__ constexpr int staging_bytes() {
   return EPI == EPI_FWD_LSE ? 0 : EPI_WARPS * STAGING_WARP_BYTES;
 }
 
-template <int EPI>
+template <int CG, int EPI>
 __host__ __device__ constexpr int gemm_smem_bytes() {
-  // 1 KB alignment slack + stages + staging + 16 barriers + tmem slot + abort flag
-  return 1024 + NUM_STAGES * STAGE_BYTES + staging_bytes<EPI>() + 256;
+  // 1 KB alignment slack + stages + staging + barriers, TMEM slot and abort flag
+  return 1024 + Cfg<CG>::NUM_STAGES * Cfg<CG>::STAGE_BYTES + staging_bytes<EPI>() + 256;
 }
 
 // Swizzled byte offset of 16-byte chunk c of row r inside a 128B-swizzled, 1 KB aligned box.
 __device__ __forceinline__ uint32_t sw128_offset(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
 // ----------------------------------------------------------------------------- kernel
-template <int EPI, bool A_MN, bool B_MN, bool HAS_CAP>
+template <int CG, int EPI, bool A_MN, bool B_MN, bool HAS_CAP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const GemmParams P) {
+  using C = Cfg<CG>;
+  constexpr int NS = C::NUM_STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
-  uint8_t* staging = smem + NUM_STAGES * STAGE_BYTES;
+  uint8_t* staging = smem + NS * C::STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(staging + staging_bytes<EPI>());
-  uint64_t* full_bar = bars;                    // [NUM_STAGES] TMA -> MMA
-  uint64_t* empty_bar = bars + NUM_STAGES;      // [NUM_STAGES] MMA -> TMA
-  uint64_t* tfull_bar = bars + 2 * NUM_STAGES;  // [2] MMA -> epilogue
-  uint64_t* tempty_bar = tfull_bar + 2;         // [2] epilogue -> MMA
-  uint64_t* done_bar = tempty_bar + 2;          // [1] MMA drain on exit
+  uint64_t* full_bar = bars;             // [NS]
+  uint64_t* empty_bar = bars + NS;       // [NS]
+  uint64_t* tfull_bar = bars + 2 * NS;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;  // [2]
+  uint64_t* done_bar = tempty_bar + 2;   // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const GemmSched& S = P.s;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;  // position in the pair
+  const bool leader = rank == 0;
+  const int unit0 = blockIdx.x / CG;                       // first unit of this CTA (pair)
+  const int unit_step = gridDim.x / CG;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NUM_STAGES; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], EPI_WARPS);
+      mbar_init(&tempty_bar[b], EPI_WARPS * CG);
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -155,11 +179,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (EPI != EPI_FWD_LSE) prefetch_tmap(&tmO);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if (CG == 2) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (CG == 2) cluster_sync(); else __syncthreads();  // barriers initialised in both CTAs
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -167,48 +196,74 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       uint32_t it = 0;
-      int last_stage_phase[NUM_STAGES];
+      int last_stage_phase[NS];
 #pragma unroll
-      for (int s = 0; s < NUM_STAGES; ++s) last_stage_phase[s] = -1;
+      for (int s = 0; s < NS; ++s) last_stage_phase[s] = -1;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < S.num_units; u += gridDim.x) {
+      for (int u = unit0; ok && u < S.num_units; u += unit_step) {
         const Unit un = get_unit(S, u);
+        const int a_row = un.m_tile * C::BM + (int)rank * 128;
         for (int nt = un.n_begin; ok && nt < un.n_begin + un.n_count; ++nt) {
+          const int b_row = nt * BN + (int)rank * C::B_ROWS;
           for (int kb = un.kb_begin; kb < un.kb_begin + un.kb_count; ++kb, ++it) {
-            const int s = it % NUM_STAGES;
-            const uint32_t ph = (it / NUM_STAGES) & 1;
+            const int s = it % NS;
+            const uint32_t ph = (it / NS) & 1;
             if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, DEV_TIMEOUT_PRODUCER)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
             last_stage_phase[s] = (int)ph;
-            uint8_t* a = stages + s * STAGE_BYTES;
+            uint8_t* a = stages + s * C::STAGE_BYTES;
             uint8_t* b = a + A_STAGE_BYTES;
             const int k0 = kb * BK;
-            if (!A_MN) {
-              tma_load_2d(a, &tmA, &full_bar[s], k0, un.m_tile * BM);
-            } else {
-              tma_load_2d(a, &tmA, &full_bar[s], un.m_tile * BM, k0);
-              tma_load_2d(a + 8192, &tmA, &full_bar[s], un.m_tile * BM + 64, k0);
-            }
-            if (!B_MN) {
-              tma_load_2d(b, &tmB, &full_bar[s], k0, nt * BN);
-            } else {
+            if constexpr (CG == 1) {
+              mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+              if (!A_MN) {
+                tma_load_2d(a, &tmA, &full_bar[s], k0, a_row);
+              } else {
+                tma_load_2d(a, &tmA, &full_bar[s], a_row, k0);
+                tma_load_2d(a + 8192, &tmA, &full_bar[s], a_row + 64, k0);
+              }
+              if (!B_MN) {
+                tma_load_2d(b, &tmB, &full_bar[s], k0, b_row);
+              } else {
 #pragma unroll
-              for (int j = 0; j < 4; ++j) tma_load_2d(b + 8192 * j, &tmB, &full_bar[s], nt * BN + 64 * j, k0);
+                for (int j = 0; j < C::B_ROWS / 64; ++j)
+                  tma_load_2d(b + 8192 * j, &tmB, &full_bar[s], b_row + 64 * j, k0);
+              }
+            } else {
+              // both CTAs' bytes land on the leader's full barrier
+              if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * C::STAGE_BYTES);
+              const uint32_t fb = mapa_shared(smem_u32(&full_bar[s]), 0);
+              if (!A_MN) {
+                tma_load_2d_pair(a, &tmA, fb, k0, a_row);
+              } else {
+                tma_load_2d_pair(a, &tmA, fb, a_row, k0);
+                tma_load_2d_pair(a + 8192, &tmA, fb, a_row + 64, k0);
+              }
+              if (!B_MN) {
+                tma_load_2d_pair(b, &tmB, fb, k0, b_row);
+              } else {
+#pragma unroll
+                for (int j = 0; j < C::B_ROWS / 64; ++j) tma_load_2d_pair(b + 8192 * j, &tmB, fb, b_row + 64 * j, k0);
+              }
             }
           }
         }
       }
-      // Never leave with TMA writes in flight into this CTA's shared memory.
-      for (int s = 0; s < NUM_STAGES; ++s) {
-        if (last_stage_phase[s] < 0) continue;
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&full_bar[s], (uint32_t)last_stage_phase[s])) {
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            record_device_error(DEV_TIMEOUT_DRAIN);
-            break;
+      // Never leave with TMA writes in flight into this CTA's shared memory. The leader's
+      // full barriers count both CTAs' bytes; in a healthy run every load was consumed by
+      // an MMA (so these waits return at once), and after a timeout the wait limit is
+      // orders of magnitude longer than any load.
+      if (leader) {
+        for (int s = 0; s < NS; ++s) {
+          if (last_stage_phase[s] < 0) continue;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full_bar[s], (uint32_t)last_stage_phase[s])) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              record_device_error(DEV_TIMEOUT_DRAIN);
+              break;
+            }
           }
         }
       }
@@ -216,11 +271,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_bf16(C::BM, BN, A_MN, B_MN);
       uint32_t it = 0, tc = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < S.num_units; u += gridDim.x) {
+      for (int u = unit0; ok && u < S.num_units; u += unit_step) {
         const Unit un = get_unit(S, u);
         for (int nt = un.n_begin; ok && nt < un.n_begin + un.n_count; ++nt, ++tc) {
           const int buf = tc & 1;
@@ -232,14 +287,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
           for (int kb = 0; kb < un.kb_count; ++kb, ++it) {
-            const int s = it % NUM_STAGES;
-            const uint32_t ph = (it / NUM_STAGES) & 1;
+            const int s = it % NS;
+            const uint32_t ph = (it / NS) & 1;
             if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, DEV_TIMEOUT_MMA)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t a_addr = smem_u32(stages + s * STAGE_BYTES);
+            const uint32_t a_addr = smem_u32(stages + s * C::STAGE_BYTES);
             const uint32_t b_addr = a_addr + A_STAGE_BYTES;
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
@@ -247,16 +302,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   A_MN ? smem_desc_sw128(a_addr + kk * 2048, 8192, 1024) : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
               const uint64_t bd =
                   B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024) : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-              mma_bf16_ss(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+              if constexpr (CG == 1)
+                mma_bf16_ss(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+              else
+                mma_bf16_ss_pair(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
             }
-            mma_commit(&empty_bar[s]);  // frees the smem stage once these MMAs have read it
+            // free the smem stage (in every CTA of the pair) once these MMAs have read it
+            if constexpr (CG == 1) {
+              mma_commit(&empty_bar[s]);
+            } else {
+              const uint32_t eb = smem_u32(&empty_bar[s]);
+              mma_commit_pair(mapa_shared(eb, 0));
+              mma_commit_pair(mapa_shared(eb, 1));
+            }
           }
           if (!ok) break;
-          mma_commit(&tfull_bar[buf]);  // accumulator ready for the epilogue
+          // accumulator ready for the epilogue warps (of every CTA of the pair)
+          if constexpr (CG == 1) {
+            mma_commit(&tfull_bar[buf]);
+          } else {
+            const uint32_t fb = smem_u32(&tfull_bar[buf]);
+            mma_commit_pair(mapa_shared(fb, 0));
+            mma_commit_pair(mapa_shared(fb, 1));
+          }
         }
       }
       // Drain: every MMA issued by this thread completes before TMEM is released.
-      mma_commit(done_bar);
+      if constexpr (CG == 1) mma_commit(done_bar); else mma_commit_pair(mapa_shared(smem_u32(done_bar), 0));
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(done_bar, 0)) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -280,9 +352,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float c2 = HAS_CAP ? cap * kLog2e : 0.f;        // c in base 2
     bool ok = true;
 
-    for (int u = blockIdx.x; ok && u < S.num_units; u += gridDim.x) {
+    for (int u = unit0; ok && u < S.num_units; u += unit_step) {
       const Unit un = get_unit(S, u);
-      const int row = un.m_tile * BM + q * 32 + lane;
+      const int row_base = un.m_tile * C::BM + (int)rank * 128 + q * 32;  // first row of this warp
+      const int row = row_base + lane;
       const bool row_ok = row < S.M;
 
       // per-row state
@@ -362,7 +435,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_wait_ld2(r0, r1);
             const int col0 = nt * BN + pc * 64;
             const int tj = yl - col0;
-            // dZ = g * (onehot - 2^(z2 - l2)) * (1 - tanh^2); packed to bf16 pairs in place
+            // dZ = g * (onehot - 2^(z2 - l2)) * (1 - tanh^2); packed to bf16 pairs
             uint32_t pk[32];
 #pragma unroll
             for (int j = 0; j < 64; j += 2) {
@@ -396,17 +469,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&tmO, buf_s, col0, un.m_tile * BM + q * 32);
+              tma_store_2d(&tmO, buf_s, col0, row_base);
               bulk_commit();
             }
             sb ^= 1;
           }
         } else {  // EPI_STORE
-          const int row0 = un.split * E.split_rows + un.m_tile * BM + q * 32;
+          const int row0 = un.split * E.split_rows + row_base;
           if (E.store_mode == STORE_BF16) {
 #pragma unroll 1
             for (int pc = 0; pc < BN / 64; ++pc) {
               uint32_t r0[32], r1[32];
+              __syncwarp();
               tmem_ld32(taddr + pc * 64, r0);
               tmem_ld32(taddr + pc * 64 + 32, r1);
               tmem_wait_ld2(r0, r1);
@@ -435,6 +509,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll 1
             for (int pc = 0; pc < BN / 32; ++pc) {
               uint32_t r[32];
+              __syncwarp();
               tmem_ld32(taddr + pc * 32, r);
               tmem_wait_ld(r);
               if (lane == 0) bulk_wait_read<1>();
@@ -458,10 +533,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
 
-        // hand the accumulator back to the MMA warp
+        // hand the accumulator back to the MMA warp (in the leader for CG = 2)
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[buf]);
+        if (lane == 0) {
+          if constexpr (CG == 1)
+            mbar_arrive(&tempty_bar[buf]);
+          else
+            mbar_arrive_remote(mapa_shared(smem_u32(&tempty_bar[buf]), 0));
+        }
       }
       if (!ok) break;
 
@@ -476,10 +556,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if (CG == 2) cluster_sync(); else __syncthreads();  // the pair's MMAs and loads are done
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (CG == 2) tmem_dealloc_pair(tmem_base, TMEM_COLS); else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 

@@ -66,6 +66,15 @@ LP_API const char* lp_last_error(void);
 /* Number of kernels this library has launched in this process (all devices). */
 LP_API long long lp_launch_count(void);
 
+/* Tensor-core CTA group of the GEMMs: 2 (default; CTA pairs on two SMs, 256x256 tiles) or
+ * 1 (single-CTA 128x256 tiles). Also settable with LP_B200_CTA_GROUP=1. Results agree to
+ * f32 rounding; the setting exists to compare the two kernels. */
+LP_API int lp_set_cta_group(int cg);
+LP_API int lp_get_cta_group(void);
+
+/* CTA pairs of the pair GEMMs that can be resident on the current device (-1 on error). */
+LP_API int lp_device_pairs(void);
+
 /* Per-kernel timing (for benchmarks): while enabled, every kernel launch of this library
  * is bracketed by CUDA events on its stream. Enabling (or disabling) clears the record. */
 LP_API int lp_profile_enable(int on);

@@ -32,6 +32,17 @@ def to_bf16(x: np.ndarray, dev) -> torch.Tensor:
     return torch.from_numpy(orc.bf16_round(x)).to(dev).to(torch.bfloat16)
 
 
+@pytest.fixture(params=[2, 1], ids=["pair", "single"])
+def cta_group(request, cuda_device):
+    """Run a test with the CTA-pair (default) and the single-CTA tensor-core GEMMs."""
+    from gemma4_posttrain_jax_b200 import _lib
+
+    before = _lib.cta_group()
+    _lib.set_cta_group(request.param)
+    yield request.param
+    _lib.set_cta_group(before)
+
+
 def _stats_case(scale, seed=20260925, V=1036, T=513, d=128):
     rng = np.random.default_rng(seed)
     w = orc.bf16_round(rng.normal(size=(V, d)) * scale)
@@ -45,7 +56,7 @@ def _stats_case(scale, seed=20260925, V=1036, T=513, d=128):
 # --------------------------------------------------------------------------- GEMM core
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 1), (1, 0)])
 @pytest.mark.parametrize("M,N,K", [(200, 300, 160), (128, 256, 64), (513, 1036, 136)])
-def test_gemm_core_matches_f32(cuda_device, a_mn, b_mn, M, N, K):
+def test_gemm_core_matches_f32(cuda_device, cta_group, a_mn, b_mn, M, N, K):
     import ctypes
 
     from gemma4_posttrain_jax_b200 import _lib
@@ -80,14 +91,14 @@ def test_gemm_core_matches_f32(cuda_device, a_mn, b_mn, M, N, K):
     got = D.cpu().numpy()
     assert np.isfinite(got).all()
     err = np.abs(got - ref).max() / max(1.0, np.abs(ref).max())
-    print(f"gemm a_mn={a_mn} b_mn={b_mn} M={M} N={N4} K={K}: max rel err {err:.2e}")
+    print(f"gemm cg={cta_group} a_mn={a_mn} b_mn={b_mn} M={M} N={N4} K={K}: max rel err {err:.2e}")
     assert err < 1e-5
 
 
 # --------------------------------------------------------------------------- forward
 @pytest.mark.parametrize("softcap", [None, 30.0])
 @pytest.mark.parametrize("scale", [0.04, 1.5])
-def test_forward_stats_and_logps(cuda_device, softcap, scale):
+def test_forward_stats_and_logps(cuda_device, cta_group, softcap, scale):
     from gemma4_posttrain_jax_b200 import ops
 
     w, h, y, _ = _stats_case(scale)
@@ -124,7 +135,7 @@ def test_forward_tails_repeated_targets_3d(cuda_device):
 # --------------------------------------------------------------------------- backward
 @pytest.mark.parametrize("softcap", [None, 30.0])
 @pytest.mark.parametrize("scale", [0.04, 1.5])
-def test_backward_matches_analytic_vjp(cuda_device, softcap, scale):
+def test_backward_matches_analytic_vjp(cuda_device, cta_group, softcap, scale):
     from gemma4_posttrain_jax_b200 import ops
 
     w, h, y, g = _stats_case(scale)
@@ -143,7 +154,7 @@ def test_backward_matches_analytic_vjp(cuda_device, softcap, scale):
 
 
 @pytest.mark.parametrize("token_chunk", [128, 256, None])
-def test_backward_token_chunks_and_bf16_outputs(cuda_device, token_chunk):
+def test_backward_token_chunks_and_bf16_outputs(cuda_device, cta_group, token_chunk):
     from gemma4_posttrain_jax_b200 import ops
 
     w, h, y, g = _stats_case(0.04)
@@ -161,7 +172,8 @@ def test_backward_token_chunks_and_bf16_outputs(cuda_device, token_chunk):
     assert rel_l2(dW16.float().cpu(), dW32.cpu()) < 5e-3
     # chunking changes only the f32 summation order of dW
     assert rel_l2(dWc.cpu(), dW32.cpu()) < 1e-5
-    assert torch.equal(dHc, dH32)
+    # ... and the split-K plan (summation order) of dH
+    assert rel_l2(dHc.cpu(), dH32.cpu()) < 1e-5
 
 
 def test_frozen_head_skips_dw(cuda_device):
@@ -180,7 +192,7 @@ def test_frozen_head_skips_dw(cuda_device):
 
 # --------------------------------------------------------------------------- vocab parallel
 @pytest.mark.parametrize("shards", [2, 4])
-def test_vocab_parallel_shards_on_one_gpu(cuda_device, shards):
+def test_vocab_parallel_shards_on_one_gpu(cuda_device, cta_group, shards):
     """Each shard through lp_fwd / lp_bwd, merged by lp_combine, equals the unsharded result.
 
     Planted per-shard maxima as in ``tests/test_sharding_tpu.py:51-61`` (seed 7), scaled to
@@ -316,7 +328,7 @@ def test_per_token_logps_autograd_and_sft(cuda_device):
     assert torch.equal(again, logps.detach())
 
 
-def test_config1_shape_fwd_bwd(cuda_device):
+def test_config1_shape_fwd_bwd(cuda_device, cta_group):
     """BASELINE config 1 at full size: T=256, d=2048, V=262144, softcap 30, seed 0."""
     from gemma4_posttrain_jax_b200 import ops
 
