@@ -132,7 +132,7 @@ def profile_read(max_tags: int = 32) -> dict[str, tuple[float, int]]:
 
 
 def set_cta_group(cg: int) -> None:
-    """Select the pair (2, default) or single-CTA (1) tensor-core GEMMs for later calls."""
+    """Force pair (2) or single-CTA (1) tensor-core GEMMs for later calls; 0 = per-GEMM default."""
     check(load().lp_set_cta_group(int(cg)), "lp_set_cta_group")
 
 

@@ -90,20 +90,32 @@ int fail(int code, const char* fmt, ...) {
 
 constexpr int kMaxDevices = 64;
 
-// Tensor-core CTA group of the GEMMs: 2 = CTA pairs with 256x256 tiles (default), 1 = single
-// CTAs with 128x256 tiles. LP_B200_CTA_GROUP=1 in the environment or lp_set_cta_group()
-// selects the single-CTA kernels (kept as the reference point of the pair kernels).
-std::atomic<int> g_cg{0};
+// Tensor-core CTA group of the GEMMs: 2 = CTA pairs with 256x256 tiles, 1 = single CTAs with
+// 128x256 tiles. By default each GEMM uses the group that measured faster for it;
+// LP_B200_CTA_GROUP=1|2 or lp_set_cta_group(1|2) forces one group for every GEMM.
+// 0 = per-GEMM default (below); 1 / 2 = force every GEMM to that CTA group.
+std::atomic<int> g_cg{-1};
 
-int cta_group() {
+int forced_cta_group() {
   int v = g_cg.load();
-  if (v == 0) {
+  if (v < 0) {
     const char* e = getenv("LP_B200_CTA_GROUP");
-    v = (e != nullptr && e[0] == '1') ? 1 : 2;
+    v = (e != nullptr && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 0;
     g_cg.store(v);
   }
   return v;
 }
+
+// CTA group per GEMM. The forward and the dZ recompute carry heavy epilogues (softcap and
+// exp per logit) and measured faster as single CTAs; the dH and dW GEMMs (plain stores)
+// measured faster as CTA pairs.
+enum CgUse { CG_FWD, CG_DZ, CG_DH, CG_DW, CG_HOOK };
+int cta_group_for(CgUse k) {
+  const int f = forced_cta_group();
+  if (f) return f;
+  return (k == CG_DH || k == CG_DW) ? 2 : 1;
+}
+int cta_group() { return forced_cta_group(); }
 
 struct DeviceInfo {
   int sms = 0;
@@ -181,7 +193,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 2-D tiled map, 128-byte swizzle, zero fill out of bounds. `inner`/`outer` in elements,
 // `row_bytes` = byte stride between outer rows.
 int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize, uint64_t inner, uint64_t outer,
-             uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, const char* what) {
+             uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, const char* what,
+             CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (fn == nullptr) return fail(LP_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
   if (inner == 0 || outer == 0) return fail(LP_EINVAL, "%s: empty tensor", what);
@@ -193,8 +206,8 @@ int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(LP_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
   return LP_OK;
 }
@@ -208,13 +221,29 @@ int map_f32(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, ui
   return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, inner, outer, ld_elems * 4, bi, bo, what);
 }
 
+// Epilogue store targets: one 32-row x 64-byte box per warp and piece, 64-byte swizzle
+// (32 bf16 or 16 f32 columns), matching the staging layout of the GEMM epilogue.
+int map_store_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+                   const char* what) {
+  return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, outer, ld_elems * 2, 32, 32, what,
+                  CU_TENSOR_MAP_SWIZZLE_64B);
+}
+int map_store_f32(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+                  const char* what) {
+  return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, inner, outer, ld_elems * 4, 16, 32, what,
+                  CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 // --------------------------------------------------------------------------- planning
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// Forward: N tiles grouped G per unit; pick the largest G within 1% of the best critical
-// path (units are dealt round-robin to `sms` persistent CTAs).
-GemmSched plan_fwd(int64_t T, int64_t Vs, int64_t d, int sms, int bm) {
+// Forward plan. The forward reads every H row block once per vocabulary tile, so the H rows
+// that concurrent CTAs re-read must stay in L2: units walk the tokens in chunks of about
+// 12288 rows (48 MB of bf16 H at d = 2048), and within a chunk all vocabulary groups
+// before the next chunk. Each unit covers G consecutive vocabulary tiles; G keeps the
+// per-row (max, sum) partials ([n_groups, T] float2) under ~128 MB.
+GemmSched plan_fwd(int64_t T, int64_t Vs, int64_t d, int workers, int bm) {
   GemmSched s{};
   s.bm = bm;
   s.M = (int)T;
@@ -226,19 +255,22 @@ GemmSched plan_fwd(int64_t T, int64_t Vs, int64_t d, int sms, int bm) {
   s.k_splits = 1;
   s.kb_per_split = s.k_blocks;
   s.n_fast = 0;
-  double best = 1e300;
-  int gmax = std::min(s.tiles_n, 256);
-  double cost[257];
-  for (int g = 1; g <= gmax; ++g) {
-    const int64_t units = (int64_t)s.tiles_m * cdiv(s.tiles_n, g);
-    cost[g] = (double)cdiv(units, sms) * g + 0.05 * g / std::max(1, s.tiles_n);
-    best = std::min(best, cost[g]);
-  }
-  int pick = 1;
-  for (int g = 1; g <= gmax; ++g)
-    if (cost[g] <= best * 1.01) pick = g;
-  s.n_group = pick;
-  s.n_groups = (int)cdiv(s.tiles_n, pick);
+  static const char* chunk_env = getenv("LP_B200_FWD_CHUNK_MB");  // tuning: H chunk size
+  const int64_t chunk_mb = (chunk_env != nullptr && atoi(chunk_env) > 0) ? atoi(chunk_env) : 48;
+  const int64_t chunk_rows = std::max<int64_t>(bm, (chunk_mb << 20) / std::max<int64_t>(2 * d, 1));
+  s.m_chunk = (int)std::max<int64_t>(1, chunk_rows / bm);
+  static const char* no_chunk = getenv("LP_B200_FWD_NO_CHUNK");  // tuning: plain M-fast order
+  if (no_chunk != nullptr && no_chunk[0] == '1') s.m_chunk = 0;
+  const int64_t part_cap = int64_t(128) << 20;
+  int g = 1;
+  while (g < s.tiles_n && 2 * cdiv(s.tiles_n, g) * T * 8 > part_cap) g *= 2;
+  // at least a few tiles per unit so the per-unit epilogue state amortises
+  g = std::max(g, std::min(4, s.tiles_n));
+  static const char* force_g = getenv("LP_B200_FWD_GROUP");  // tuning: tiles per unit
+  if (force_g != nullptr && atoi(force_g) > 0) g = std::min(atoi(force_g), s.tiles_n);
+  (void)workers;
+  s.n_group = g;
+  s.n_groups = (int)cdiv(s.tiles_n, g);
   s.num_units = s.tiles_m * s.n_groups;
   return s;
 }
@@ -260,10 +292,14 @@ GemmSched plan_gemm(int64_t M, int64_t N, int64_t K, int sms, bool allow_split, 
   const int64_t tiles = (int64_t)s.tiles_m * s.tiles_n;
   int best_s = 1;
   double best = 1e300;
-  const int smax = allow_split ? 16 : 1;
+  const int smax = allow_split ? 64 : 1;
+  // Concurrent units stream shared operands through L2; a unit longer than ~1024 K blocks
+  // lets CTAs drift apart by more than L2 holds, so long K ranges are split.
+  const int64_t kb_cap = 1024;
   for (int sp = 1; sp <= smax; ++sp) {
     const int64_t kb = cdiv(s.k_blocks, sp);
     if (sp > 1 && kb < 8) break;
+    if (allow_split && kb > kb_cap) continue;
     const int64_t real_splits = cdiv(s.k_blocks, kb);
     if (real_splits != sp) continue;
     const double c = (double)cdiv(tiles * sp, sms) * kb * (1.0 + 0.02 * (sp > 1));
@@ -371,6 +407,32 @@ int launch_gemm_cap(bool cap, cudaStream_t st, const CUtensorMap& a, const CUten
              : launch_gemm<EPI, A_MN, B_MN, false>(st, a, b, o, p, di, tag);
 }
 
+// L2 eviction priorities of the A / B loads of each GEMM (0 normal = plain load,
+// 1 evict_first, 2 evict_last). Measured (ncu DRAM bytes per launch at the config-2 size):
+// plain loads keep the forward and the dZ recompute near their algorithmic traffic;
+// evict_first on an operand that concurrent CTAs share (W) multiplies HBM reads, and an
+// explicit evict_normal policy is not the same as no hint. The dW GEMM keeps its H chunk
+// (re-read by every vocabulary tile) with evict_last. LP_B200_L2HINTS="fA fB zA zB hA hB wA wB" (8 digits: forward,
+// dZ recompute, dH, dW) overrides them for tuning.
+enum GemmKind { G_FWD = 0, G_DZ = 1, G_DH = 2, G_DW = 3 };
+int l2_hint(GemmKind k, int operand) {
+  static int table[8] = {0, 0, 0, 0, 0, 0, 0, 2};
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* e = getenv("LP_B200_L2HINTS");
+    if (e == nullptr) return;
+    int i = 0;
+    for (const char* c = e; *c && i < 8; ++c)
+      if (*c >= '0' && *c <= '2') table[i++] = *c - '0';
+  });
+  return table[2 * (int)k + operand];
+}
+
+void set_hints(GemmParams& p, GemmKind k) {
+  p.e.a_l2 = l2_hint(k, 0);
+  p.e.b_l2 = l2_hint(k, 1);
+}
+
 // Box height of a K-major B operand: the rows of B one CTA stages.
 uint32_t b_box_rows(int cg) { return (uint32_t)(BN / cg); }
 
@@ -402,7 +464,7 @@ int lp_device_pairs(void) {
 }
 
 int lp_set_cta_group(int cg) {
-  if (cg != 1 && cg != 2) return fail(LP_EINVAL, "cta group must be 1 or 2, got %d", cg);
+  if (cg != 0 && cg != 1 && cg != 2) return fail(LP_EINVAL, "cta group must be 0, 1 or 2, got %d", cg);
   g_cg.store(cg);
   return LP_OK;
 }
@@ -468,9 +530,9 @@ size_t lp_fwd_workspace_bytes(int64_t T, int64_t Vs) {
   int sms = 148;
   if (current_device_info(&di) == LP_OK) sms = di->sms;
   if (T <= 0 || Vs <= 0) return 256;
-  const int cg = cta_group();
+  const int cg = cta_group_for(CG_FWD);
   GemmSched s = plan_fwd(T, Vs, 64, di != nullptr ? workers(di, cg) : (cg == 1 ? sms : sms / 2), 128 * cg);
-  return align_up((size_t)s.n_groups * T * sizeof(float2), 256) + align_up((size_t)T * 4, 256);
+  return align_up((size_t)2 * s.n_groups * T * sizeof(float2), 256) + align_up((size_t)T * 4, 256);
 }
 
 int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
@@ -482,9 +544,9 @@ int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
   DeviceInfo* di = nullptr;
   if ((rc = current_device_info(&di))) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int cg = cta_group();
+  const int cg = cta_group_for(CG_FWD);
   GemmSched s = plan_fwd(T, Vs, d, workers(di, cg), 128 * cg);
-  const size_t part_bytes = align_up((size_t)s.n_groups * T * sizeof(float2), 256);
+  const size_t part_bytes = align_up((size_t)2 * s.n_groups * T * sizeof(float2), 256);
   const size_t need = part_bytes + align_up((size_t)T * 4, 256);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(LP_EWORKSPACE, "lp_fwd needs %zu workspace bytes, got %zu", need, workspace_bytes);
@@ -501,9 +563,11 @@ int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
   p.e.softcap = softcap;
   p.e.part = part;
   p.e.tgt = tgt;
+  set_hints(p, G_FWD);
   if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di, "fwd_lse_gemm"))) return rc;
   ProfScope prof(st, "fwd_finalize");
-  fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, s.n_groups, (int)T, tgt, y, v_off, Vs, stats, logp);
+  fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, 2 * s.n_groups, (int)T, tgt, y, v_off, Vs, stats,
+                                                              logp);
   LP_LAUNCH_CHECK("fwd_finalize_kernel");
   return LP_OK;
 }
@@ -524,7 +588,7 @@ size_t lp_bwd_workspace_bytes(int64_t T, int64_t d, int64_t Vs, int64_t token_ch
   int sms = 148;
   if (current_device_info(&di) == LP_OK) sms = di->sms;
   if (T <= 0 || Vs <= 0 || d <= 0) return 256;
-  const int cg = cta_group();
+  const int cg = cta_group_for(CG_DH);  // the split-K partials follow the dH GEMM's tiles
   return bwd_layout(T, d, Vs, token_chunk, flags, di != nullptr ? workers(di, cg) : (cg == 1 ? sms : sms / 2),
                     128 * cg).total +
          256;
@@ -549,9 +613,8 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
     if (want_dw) LP_CUDA_TRY(cudaMemsetAsync(dW, 0, (size_t)Vs * d * (dw_bf16 ? 2 : 4), st));
     return LP_OK;
   }
-  const int cg = cta_group();
-  const int bm = 128 * cg, nw = workers(di, cg);
-  const BwdLayout L = bwd_layout(T, d, Vs, token_chunk, flags, nw, bm);
+  const int cg_dz = cta_group_for(CG_DZ), cg_dh = cta_group_for(CG_DH), cg_dw = cta_group_for(CG_DW);
+  const BwdLayout L = bwd_layout(T, d, Vs, token_chunk, flags, workers(di, cg_dh), 128 * cg_dh);
   if (workspace == nullptr || workspace_bytes < L.total)
     return fail(LP_EWORKSPACE, "lp_bwd needs %zu workspace bytes, got %zu", L.total, workspace_bytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & 1023) != 0) return fail(LP_EINVAL, "workspace must be 1024-byte aligned");
@@ -572,16 +635,17 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
     {
       alignas(64) CUtensorMap ta, tb, to;
       if ((rc = map_bf16(&ta, Hc, d, tcur, ldh, BK, 128, "hidden chunk"))) return rc;
-      if ((rc = map_bf16(&tb, W, d, Vs, d, BK, b_box_rows(cg), "embedding"))) return rc;
-      if ((rc = map_bf16(&to, dz, Vs, tcur, L.ldz, 64, 32, "dZ store"))) return rc;
+      if ((rc = map_bf16(&tb, W, d, Vs, d, BK, b_box_rows(cg_dz), "embedding"))) return rc;
+      if ((rc = map_store_bf16(&to, dz, Vs, tcur, L.ldz, "dZ store"))) return rc;
       GemmParams p{};
-      p.s = plan_gemm(tcur, Vs, d, nw, false, 0, bm);
+      p.s = plan_gemm(tcur, Vs, d, workers(di, cg_dz), false, 0, 128 * cg_dz);
       p.e.y = y + t0;
       p.e.v_off = v_off;
       p.e.softcap = softcap;
       p.e.g = g + t0;
       p.e.stats = norm + t0;
       p.e.stats_ld = T;
+      set_hints(p, G_DZ);
       if ((rc = launch_gemm_cap<EPI_BWD_DZ, false, false>(cap, st, ta, tb, to, p, di, "bwd_dz_gemm"))) return rc;
     }
     // 2) dH[t0:t0+tcur] = dZ . W
@@ -590,22 +654,23 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
       if ((rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, BK, 128, "dZ as A"))) return rc;
       if ((rc = map_bf16(&tb, W, d, Vs, d, 64, 64, "embedding as MN-major B"))) return rc;
       GemmParams p{};
-      p.s = plan_gemm(tcur, d, Vs, nw, true, 1, bm);
+      p.s = plan_gemm(tcur, d, Vs, workers(di, cg_dh), true, 1, 128 * cg_dh);
       char* dh_c = reinterpret_cast<char*>(dH) + (size_t)t0 * ld_dh * (dh_f32 ? 4 : 2);
       if (p.s.k_splits == 1) {
         if (dh_f32) {
-          if ((rc = map_f32(&to, dh_c, d, tcur, ld_dh, 32, 32, "dH store"))) return rc;
+          if ((rc = map_store_f32(&to, dh_c, d, tcur, ld_dh, "dH store"))) return rc;
           p.e.store_mode = STORE_F32;
         } else {
-          if ((rc = map_bf16(&to, dh_c, d, tcur, ld_dh, 64, 32, "dH store"))) return rc;
+          if ((rc = map_store_bf16(&to, dh_c, d, tcur, ld_dh, "dH store"))) return rc;
           p.e.store_mode = STORE_BF16;
         }
         p.e.split_rows = 0;
       } else {
-        if ((rc = map_f32(&to, part, d, (uint64_t)p.s.k_splits * L.mpad, d, 32, 32, "dH partials"))) return rc;
+        if ((rc = map_store_f32(&to, part, d, (uint64_t)p.s.k_splits * L.mpad, d, "dH partials"))) return rc;
         p.e.store_mode = STORE_F32;
         p.e.split_rows = (int)L.mpad;
       }
+      set_hints(p, G_DH);
       if ((rc = launch_gemm<EPI_STORE, false, true, false>(st, ta, tb, to, p, di, "bwd_dh_gemm"))) return rc;
       if (p.s.k_splits > 1) {
         const int64_t total = tcur * (d / 4);
@@ -621,15 +686,16 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
       if ((rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, 64, 64, "dZ as MN-major A"))) return rc;
       if ((rc = map_bf16(&tb, Hc, d, tcur, ldh, 64, 64, "hidden as MN-major B"))) return rc;
       GemmParams p{};
-      p.s = plan_gemm(Vs, d, tcur, nw, false, 1, bm);
+      p.s = plan_gemm(Vs, d, tcur, workers(di, cg_dw), false, 1, 128 * cg_dw);
       const bool direct_bf16 = dw_bf16 && L.chunks == 1;
       if (direct_bf16) {
-        if ((rc = map_bf16(&to, dW, d, Vs, d, 64, 32, "dW store"))) return rc;
+        if ((rc = map_store_bf16(&to, dW, d, Vs, d, "dW store"))) return rc;
         p.e.store_mode = STORE_BF16;
       } else {
-        if ((rc = map_f32(&to, dw_acc, d, Vs, d, 32, 32, "dW store"))) return rc;
+        if ((rc = map_store_f32(&to, dw_acc, d, Vs, d, "dW store"))) return rc;
         p.e.store_mode = c == 0 ? STORE_F32 : STORE_F32_ADD;
       }
+      set_hints(p, G_DW);
       if ((rc = launch_gemm<EPI_STORE, true, true, false>(st, ta, tb, to, p, di, "bwd_dw_gemm"))) return rc;
     }
   }
@@ -658,11 +724,11 @@ int lp_gemm_bf16(void* stream, const void* A, int64_t M, int64_t K, int64_t lda,
   if (a_mn) rc = map_bf16(&ta, A, M, K, lda, 64, 64, "A (MN-major)");
   else rc = map_bf16(&ta, A, K, M, lda, BK, 128, "A (K-major)");
   if (rc) return rc;
-  const int cg = cta_group();
+  const int cg = cta_group_for(CG_HOOK);
   if (b_mn) rc = map_bf16(&tb, B, N, K, ldb, 64, 64, "B (MN-major)");
   else rc = map_bf16(&tb, B, K, N, ldb, BK, b_box_rows(cg), "B (K-major)");
   if (rc) return rc;
-  if ((rc = map_f32(&to, D, N, M, ldd, 32, 32, "D"))) return rc;
+  if ((rc = map_store_f32(&to, D, N, M, ldd, "D"))) return rc;
   GemmParams p{};
   p.s = plan_gemm(M, N, K, workers(di, cg), false, 0, 128 * cg);
   p.e.store_mode = STORE_F32;
@@ -793,7 +859,7 @@ int noalloc_scratch(void** out) {
 }
 
 size_t noalloc_fwd_bytes(const GemmSched& s, int64_t T, size_t* part_bytes) {
-  *part_bytes = align_up((size_t)s.n_groups * T * sizeof(float2), 256);
+  *part_bytes = align_up((size_t)2 * s.n_groups * T * sizeof(float2), 256);
   return *part_bytes + align_up((size_t)T * 4, 256);
 }
 
@@ -809,7 +875,7 @@ extern "C" int lp_fwd_noalloc(void* stream, const void* H, int64_t T, int64_t d,
   if ((rc = current_device_info(&di))) return rc;
   // Same tile plan as lp_fwd, with the vocabulary groups widened until the partials fit
   // the fixed scratch; too many tokens for even one group is refused.
-  const int cg = cta_group();
+  const int cg = cta_group_for(CG_FWD);
   GemmSched s = plan_fwd(T, Vs, d, workers(di, cg), 128 * cg);
   size_t part_bytes = 0;
   while (noalloc_fwd_bytes(s, T, &part_bytes) > kNoAllocScratchBytes && s.n_group < s.tiles_n) {
@@ -839,9 +905,11 @@ extern "C" int lp_fwd_noalloc(void* stream, const void* H, int64_t T, int64_t d,
   p.e.softcap = softcap;
   p.e.part = part;
   p.e.tgt = tgt;
+  set_hints(p, G_FWD);
   if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di, "fwd_lse_gemm"))) return rc;
   ProfScope prof(st, "fwd_finalize");
-  fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, s.n_groups, (int)T, tgt, y, v_off, Vs, stats, logp);
+  fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, 2 * s.n_groups, (int)T, tgt, y, v_off, Vs, stats,
+                                                              logp);
   LP_LAUNCH_CHECK("fwd_finalize_kernel");
   return LP_OK;
 }

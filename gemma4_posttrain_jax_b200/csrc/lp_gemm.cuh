@@ -15,7 +15,8 @@
 //
 //   warp 0      : TMA producer (one thread)  -> NUM_STAGES-deep smem ring
 //   warp 1      : TMEM allocator + MMA issuer (one thread; in the pair leader only)
-//   warps 2..5  : epilogue; warp w reads TMEM lanes 32*(w%4).. (its 32 rows of the tile)
+//   warps 2..9  : epilogue; warp w reads TMEM lanes 32*(w%4).. (its 32 rows of the tile) and
+//                 one half (128 columns) of the tile; two epilogue warps per SM sub-partition
 //
 // The two 256-column f32 accumulators (512 TMEM columns) are double-buffered, so the
 // epilogue of tile i overlaps the MMAs of tile i+1. Operands are K-major or MN-major,
@@ -23,7 +24,7 @@
 //
 // Epilogues:
 //   EPI_FWD_LSE : softcap + running (max, sum-exp) per row in base 2 + target pick, never
-//                 writing logits; one (max, sum) partial per row per unit.
+//                 writing logits; one (max, sum) partial per row per unit and column half.
 //   EPI_BWD_DZ  : recompute path; dZ = g * (onehot - softmax) * softcap' written as bf16
 //                 through swizzled smem staging + TMA store.
 //   EPI_STORE   : plain f32 / bf16 store or f32 TMA reduce-add of the accumulator.
@@ -41,11 +42,11 @@ namespace lpk {
 
 constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int A_STAGE_BYTES = 128 * BK * 2;                // 16 KB: 128 rows of A per CTA
-constexpr int STAGING_BUF_BYTES = 32 * 128;                // 32 rows x 128 B, one TMA box
+constexpr int STAGING_BUF_BYTES = 32 * 64;                 // 32 rows x 64 B, one TMA box
 constexpr int STAGING_WARP_BYTES = 2 * STAGING_BUF_BYTES;  // double-buffered per warp
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -70,6 +71,8 @@ struct GemmSched {
   int num_units;
   int n_fast;  // 1: consecutive units step through N groups first (share the A tile)
   int bm;      // rows per M tile (128 * CG)
+  int m_chunk; // > 0 (with n_fast = 0): units walk M in chunks of m_chunk tiles, all N groups
+               // of a chunk before the next chunk, so the A rows CTAs re-read stay in L2
 };
 
 struct EpiParams {
@@ -83,6 +86,7 @@ struct EpiParams {
   long long stats_ld;    // DZ : row stride of stats
   int store_mode;        // STORE: STORE_BF16 / STORE_F32 / STORE_F32_ADD
   int split_rows;        // STORE: output-row offset between K splits (partials)
+  int a_l2, b_l2;        // L2 eviction priority of the A / B loads (L2_NORMAL / _EVICT_FIRST / _EVICT_LAST)
 };
 
 struct GemmParams {
@@ -98,7 +102,23 @@ struct Unit {
 
 __device__ __forceinline__ Unit get_unit(const GemmSched& s, int u) {
   int m, g, ks;
-  if (s.n_fast) {
+  if (!s.n_fast && s.m_chunk > 0) {
+    // chunk-major: (chunk, N group, M tile within the chunk); the last chunk may be short
+    const int mc = s.m_chunk;
+    const int full = s.tiles_m / mc;
+    const int per_chunk = mc * s.n_groups;
+    if (u < full * per_chunk) {
+      const int c = u / per_chunk, r = u % per_chunk;
+      g = r / mc;
+      m = c * mc + r % mc;
+    } else {
+      const int lm = s.tiles_m - full * mc;
+      const int r = u - full * per_chunk;
+      g = r / lm;
+      m = full * mc + r % lm;
+    }
+    ks = 0;
+  } else if (s.n_fast) {
     g = u % s.n_groups;
     const int r = u / s.n_groups;
     m = r % s.tiles_m;
@@ -131,8 +151,9 @@ __host__ __device__ constexpr int gemm_smem_bytes() {
   return 1024 + Cfg<CG>::NUM_STAGES * Cfg<CG>::STAGE_BYTES + staging_bytes<EPI>() + 256;
 }
 
-// Swizzled byte offset of 16-byte chunk c of row r inside a 128B-swizzled, 1 KB aligned box.
-__device__ __forceinline__ uint32_t sw128_offset(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+// Byte offset of 16-byte chunk c (0..3) of row r in a 64-byte-swizzled box of 64-byte rows
+// (the TMA SWIZZLE_64B pattern: address bits [4,6) ^= bits [7,9)); 512-byte aligned box.
+__device__ __forceinline__ uint32_t sw64_offset(int r, int c) { return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
 
 // ----------------------------------------------------------------------------- kernel
 template <int CG, int EPI, bool A_MN, bool B_MN, bool HAS_CAP>
@@ -195,6 +216,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
+      // plain loads unless a priority was asked for (an explicit evict_normal policy is not
+      // the same as no hint)
+      const bool hint_a = P.e.a_l2 != L2_NORMAL, hint_b = P.e.b_l2 != L2_NORMAL;
+      const uint64_t pol_a = hint_a ? make_l2_policy(P.e.a_l2) : 0;
+      const uint64_t pol_b = hint_b ? make_l2_policy(P.e.b_l2) : 0;
+      auto ld1 = [&](void* dst, const CUtensorMap* m, uint64_t* bar, int x, int y, bool h, uint64_t pol) {
+        if (h) tma_load_2d_hint(dst, m, bar, x, y, pol); else tma_load_2d(dst, m, bar, x, y);
+      };
+      auto ld2 = [&](void* dst, const CUtensorMap* m, uint32_t bar, int x, int y, bool h, uint64_t pol) {
+        if (h) tma_load_2d_pair_hint(dst, m, bar, x, y, pol); else tma_load_2d_pair(dst, m, bar, x, y);
+      };
       uint32_t it = 0;
       int last_stage_phase[NS];
 #pragma unroll
@@ -219,33 +251,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if constexpr (CG == 1) {
               mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
               if (!A_MN) {
-                tma_load_2d(a, &tmA, &full_bar[s], k0, a_row);
+                ld1(a, &tmA, &full_bar[s], k0, a_row, hint_a, pol_a);
               } else {
-                tma_load_2d(a, &tmA, &full_bar[s], a_row, k0);
-                tma_load_2d(a + 8192, &tmA, &full_bar[s], a_row + 64, k0);
+                ld1(a, &tmA, &full_bar[s], a_row, k0, hint_a, pol_a);
+                ld1(a + 8192, &tmA, &full_bar[s], a_row + 64, k0, hint_a, pol_a);
               }
               if (!B_MN) {
-                tma_load_2d(b, &tmB, &full_bar[s], k0, b_row);
+                ld1(b, &tmB, &full_bar[s], k0, b_row, hint_b, pol_b);
               } else {
 #pragma unroll
                 for (int j = 0; j < C::B_ROWS / 64; ++j)
-                  tma_load_2d(b + 8192 * j, &tmB, &full_bar[s], b_row + 64 * j, k0);
+                  ld1(b + 8192 * j, &tmB, &full_bar[s], b_row + 64 * j, k0, hint_b, pol_b);
               }
             } else {
               // both CTAs' bytes land on the leader's full barrier
               if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * C::STAGE_BYTES);
               const uint32_t fb = mapa_shared(smem_u32(&full_bar[s]), 0);
               if (!A_MN) {
-                tma_load_2d_pair(a, &tmA, fb, k0, a_row);
+                ld2(a, &tmA, fb, k0, a_row, hint_a, pol_a);
               } else {
-                tma_load_2d_pair(a, &tmA, fb, a_row, k0);
-                tma_load_2d_pair(a + 8192, &tmA, fb, a_row + 64, k0);
+                ld2(a, &tmA, fb, a_row, k0, hint_a, pol_a);
+                ld2(a + 8192, &tmA, fb, a_row + 64, k0, hint_a, pol_a);
               }
               if (!B_MN) {
-                tma_load_2d_pair(b, &tmB, fb, k0, b_row);
+                ld2(b, &tmB, fb, k0, b_row, hint_b, pol_b);
               } else {
 #pragma unroll
-                for (int j = 0; j < C::B_ROWS / 64; ++j) tma_load_2d_pair(b + 8192 * j, &tmB, fb, b_row + 64 * j, k0);
+                for (int j = 0; j < C::B_ROWS / 64; ++j) ld2(b + 8192 * j, &tmB, fb, b_row + 64 * j, k0, hint_b, pol_b);
               }
             }
           }
@@ -340,8 +372,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ epilogue warps
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // Two warps per TMEM lane quarter: warp 2+e (e = 0..7) reads lanes 32*(warp%4).. and
+    // columns [128*h, 128*h + 128) of every tile, h = e / 4.
+    const int q = warp & 3;
     const int ew = warp - 2;
+    const int h = ew / 4;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     uint8_t* my_staging = staging + ew * STAGING_WARP_BYTES;
     int sb = 0;
@@ -385,17 +420,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t taddr = tmem_base + lane_base + (uint32_t)(buf * BN);
+        const uint32_t taddr = tmem_base + lane_base + (uint32_t)(buf * BN + h * (BN / 2));
+        const int colh = nt * BN + h * (BN / 2);  // first column of this warp's half
 
         if constexpr (EPI == EPI_FWD_LSE) {
 #pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
+          for (int c = 0; c < BN / 64; ++c) {
             uint32_t r[32];
             __syncwarp();
             tmem_ld32(taddr + c * 32, r);
             tmem_wait_ld(r);
-            const int col0 = nt * BN + c * 32;
-            const int nvalid = S.N - col0;  // columns >= nvalid are vocabulary padding
+            const int col0 = colh + c * 32;
+            const int nvalid = S.N - col0;  // columns >= nvalid are vocabulary padding (warp-uniform)
+            if (nvalid <= 0) continue;
             float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -428,22 +465,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         } else if constexpr (EPI == EPI_BWD_DZ) {
 #pragma unroll 1
           for (int pc = 0; pc < BN / 64; ++pc) {
-            uint32_t r0[32], r1[32];
+            uint32_t r[32];
             __syncwarp();
-            tmem_ld32(taddr + pc * 64, r0);
-            tmem_ld32(taddr + pc * 64 + 32, r1);
-            tmem_wait_ld2(r0, r1);
-            const int col0 = nt * BN + pc * 64;
+            tmem_ld32(taddr + pc * 32, r);
+            tmem_wait_ld(r);
+            const int col0 = colh + pc * 32;
             const int tj = yl - col0;
             // dZ = g * (onehot - 2^(z2 - l2)) * (1 - tanh^2); packed to bf16 pairs
-            uint32_t pk[32];
+            uint32_t pk[16];
 #pragma unroll
-            for (int j = 0; j < 64; j += 2) {
+            for (int j = 0; j < 32; j += 2) {
               float v[2];
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int jj = j + h;
-                const float x = __uint_as_float(jj < 32 ? r0[jj] : r1[jj - 32]);
+              for (int hh = 0; hh < 2; ++hh) {
+                const int jj = j + hh;
+                const float x = __uint_as_float(r[jj]);
                 float z, chain;
                 if (HAS_CAP) {
                   const float rr = fast_rcp(1.f + fast_ex2(x * k1));
@@ -455,7 +491,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 const float p = fast_ex2(z - l2);
                 const float onehot = (jj == tj) ? 1.f : 0.f;
-                v[h] = gv * chain * (onehot - p);
+                v[hh] = gv * chain * (onehot - p);
               }
               pk[j >> 1] = pack_bf16x2(v[0], v[1]);
             }
@@ -464,8 +500,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
             const uint32_t sbase = smem_u32(buf_s);
 #pragma unroll
-            for (int c = 0; c < 8; ++c)
-              st_shared_v4(sbase + sw128_offset(lane, c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            for (int c = 0; c < 4; ++c)
+              st_shared_v4(sbase + sw64_offset(lane, c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -479,28 +515,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (E.store_mode == STORE_BF16) {
 #pragma unroll 1
             for (int pc = 0; pc < BN / 64; ++pc) {
-              uint32_t r0[32], r1[32];
+              uint32_t r[32];
               __syncwarp();
-              tmem_ld32(taddr + pc * 64, r0);
-              tmem_ld32(taddr + pc * 64 + 32, r1);
-              tmem_wait_ld2(r0, r1);
-              uint32_t pk[32];
+              tmem_ld32(taddr + pc * 32, r);
+              tmem_wait_ld(r);
+              uint32_t pk[16];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(r0[2 * j]), __uint_as_float(r0[2 * j + 1]));
-#pragma unroll
-              for (int j = 0; j < 16; ++j)
-                pk[16 + j] = pack_bf16x2(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1]));
+              for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
               if (lane == 0) bulk_wait_read<1>();
               __syncwarp();
               uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
               const uint32_t sbase = smem_u32(buf_s);
 #pragma unroll
-              for (int c = 0; c < 8; ++c)
-                st_shared_v4(sbase + sw128_offset(lane, c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+              for (int c = 0; c < 4; ++c)
+                st_shared_v4(sbase + sw64_offset(lane, c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
               fence_proxy_async_smem();
               __syncwarp();
               if (lane == 0) {
-                tma_store_2d(&tmO, buf_s, nt * BN + pc * 64, row0);
+                tma_store_2d(&tmO, buf_s, colh + pc * 32, row0);
                 bulk_commit();
               }
               sb ^= 1;
@@ -508,24 +540,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           } else {
 #pragma unroll 1
             for (int pc = 0; pc < BN / 32; ++pc) {
-              uint32_t r[32];
+              uint32_t r[16];
               __syncwarp();
-              tmem_ld32(taddr + pc * 32, r);
-              tmem_wait_ld(r);
+              tmem_ld16(taddr + pc * 16, r);
+              tmem_wait_ld16(r);
               if (lane == 0) bulk_wait_read<1>();
               __syncwarp();
               uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
               const uint32_t sbase = smem_u32(buf_s);
 #pragma unroll
-              for (int c = 0; c < 8; ++c)
-                st_shared_v4(sbase + sw128_offset(lane, c), r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+              for (int c = 0; c < 4; ++c)
+                st_shared_v4(sbase + sw64_offset(lane, c), r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
               fence_proxy_async_smem();
               __syncwarp();
               if (lane == 0) {
                 if (E.store_mode == STORE_F32_ADD)
-                  tma_reduce_add_2d(&tmO, buf_s, nt * BN + pc * 32, row0);
+                  tma_reduce_add_2d(&tmO, buf_s, colh + pc * 16, row0);
                 else
-                  tma_store_2d(&tmO, buf_s, nt * BN + pc * 32, row0);
+                  tma_store_2d(&tmO, buf_s, colh + pc * 16, row0);
                 bulk_commit();
               }
               sb ^= 1;
@@ -546,7 +578,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!ok) break;
 
       if constexpr (EPI == EPI_FWD_LSE) {
-        if (row_ok) E.part[(size_t)un.group * S.M + row] = make_float2(run_m, run_s);
+        // one (max, sum) partial per unit and column half
+        if (row_ok) E.part[(size_t)(un.group * 2 + h) * S.M + row] = make_float2(run_m, run_s);
       }
     }
     if (EPI != EPI_FWD_LSE) {

@@ -7,7 +7,8 @@
 
 namespace lpk {
 
-// Merge the per-unit (max2, sum) partials of every vocab group of one shard.
+// Merge the per-unit (max2, sum) partials of every vocab group (and column half) of one
+// shard. A partial of a half that saw only vocabulary padding is (-inf, 0) and adds 0.
 //   stats[0][t] = max (natural units), stats[1][t] = sum exp(z - max),
 //   stats[2][t] = owned target logit or 0;  logp[t] = stats[2] - (max + log sum)
 __global__ void fwd_finalize_kernel(const float2* __restrict__ part, int n_groups, int T,

@@ -66,9 +66,11 @@ LP_API const char* lp_last_error(void);
 /* Number of kernels this library has launched in this process (all devices). */
 LP_API long long lp_launch_count(void);
 
-/* Tensor-core CTA group of the GEMMs: 2 (default; CTA pairs on two SMs, 256x256 tiles) or
- * 1 (single-CTA 128x256 tiles). Also settable with LP_B200_CTA_GROUP=1. Results agree to
- * f32 rounding; the setting exists to compare the two kernels. */
+/* Tensor-core CTA group of the GEMMs: 0 (default) lets each GEMM use the group measured
+ * faster for it (single CTAs, 128x256 tiles, for the forward and the dZ recompute; CTA pairs
+ * on two SMs, 256x256 tiles, for dH and dW); 1 or 2 forces one group for every GEMM (also
+ * LP_B200_CTA_GROUP=1|2). Results agree to f32 rounding; lp_get_cta_group() returns the
+ * forced group or 0. */
 LP_API int lp_set_cta_group(int cg);
 LP_API int lp_get_cta_group(void);
 

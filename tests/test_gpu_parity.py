@@ -32,9 +32,9 @@ def to_bf16(x: np.ndarray, dev) -> torch.Tensor:
     return torch.from_numpy(orc.bf16_round(x)).to(dev).to(torch.bfloat16)
 
 
-@pytest.fixture(params=[2, 1], ids=["pair", "single"])
+@pytest.fixture(params=[0, 2, 1], ids=["default", "pair", "single"])
 def cta_group(request, cuda_device):
-    """Run a test with the CTA-pair (default) and the single-CTA tensor-core GEMMs."""
+    """Run a test with the per-GEMM default, all-pair and all-single tensor-core GEMMs."""
     from gemma4_posttrain_jax_b200 import _lib
 
     before = _lib.cta_group()
