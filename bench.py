@@ -281,6 +281,9 @@ def main():
     softcap = args.softcap if args.softcap > 0 else None
     prompt_len, resp_len, mask_np, ids_np, g_np = make_batch(args.batch)
     n_valid = int(mask_np.sum())
+    # rows the backward computes: valid tokens with nonzero dlogp (zero-gradient rows are
+    # skipped by the library, as the reference's Pallas backward skips all-zero blocks)
+    n_bwd = int((g_np[mask_np] != 0).sum())
     vs = V // world
 
     # inputs: the same seeded draws on every rank; each rank keeps its W row block
@@ -319,7 +322,10 @@ def main():
     assert _lib.device_error(local) == 0, "device-side error during warm-up"
     barrier()
     torch.cuda.synchronize()
+    from gemma4_posttrain_jax_b200 import phase_timer
+
     _lib.profile_enable(True)
+    phase_timer.enable(True)
     launches0 = _lib.launch_count()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(list(range(world))) as clocks:
@@ -333,6 +339,8 @@ def main():
     launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
     prof = _lib.profile_read()
     _lib.profile_enable(False)
+    phases = phase_timer.read()
+    phase_timer.enable(False)
     ms = max_over_ranks(start.elapsed_time(stop) / args.steps)
     value = n_valid / (ms / 1e3)
     clock_summary = clocks.summary() if rank == 0 else None
@@ -379,9 +387,9 @@ def main():
     peaks, peak_src = load_peaks()
     flops_per_step = {
         "fwd_lse_gemm": 2.0 * n_valid * D * vs,
-        "bwd_dz_gemm": 2.0 * n_valid * D * vs,
-        "bwd_dh_gemm": 2.0 * n_valid * D * vs,
-        "bwd_dw_gemm": 2.0 * n_valid * D * vs,
+        "bwd_dz_gemm": 2.0 * n_bwd * D * vs,
+        "bwd_dh_gemm": 2.0 * n_bwd * D * vs,
+        "bwd_dw_gemm": 2.0 * n_bwd * D * vs,
     }
     kernels = {}
     for name, (tot_ms, cnt) in prof.items():
@@ -410,8 +418,9 @@ def main():
             "peak_source": f"bf16_tflops_sustained ({peak_src}); kernel runs inside a long step",
             "flop_per_launch": flop_per_launch,
         }
-    total_flops = 8.0 * n_valid * D * V
+    total_flops = 2.0 * n_valid * D * V + 6.0 * n_bwd * D * V  # the GEMM work one step needs
     step_tflops = total_flops / (ms / 1e3) / 1e12
+    dense_equiv_tflops = 8.0 * n_valid * D * V / (ms / 1e3) / 1e12  # the 8*T*d*V roofline's count
 
     # ---------------------------------------------------------------- CPU baseline (rank 0, N = 1)
     cpu = None
@@ -449,7 +458,11 @@ def main():
             "cpu_baseline": cpu,
             "step_tflops": step_tflops,
             "step_frac_of_sustained_peak": step_tflops / world / peaks["bf16_tflops_sustained"],
+            "dense_8Tdv_tflops": dense_equiv_tflops,
+            "backward_rows": n_bwd,
             "kernels": kernels,
+            "host_phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
+            "kernel_ms_per_step": sum(v["ms_per_step"] for v in kernels.values()),
             "cta_group": cta_group_of_run(),
         }
         print(json.dumps(line), flush=True)

@@ -58,7 +58,9 @@ _SIG = {
         [_P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t],
     ),
     "lp_gemm_bf16": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, ctypes.c_int, _P, _I64, _I64, ctypes.c_int, _P, _I64]),
-    "lp_scatter_rows": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _I64, ctypes.c_int, _P, _I64, _I64, _I64]),
+    "lp_scatter_rows": (
+        ctypes.c_int, [_P, _P, _I64, _P, _I64, _I64, ctypes.c_int, _P, _I64, _I64, _I64, ctypes.c_int]
+    ),
 }
 EXPORTED_SYMBOLS = tuple(_SIG)
 

@@ -792,13 +792,27 @@ int lp_compact(void* stream, const uint8_t* mask, int64_t B, int64_t N, const vo
 
 int lp_scatter_rows(void* stream, const void* src, int64_t src_stride, const int32_t* pos, int64_t slots,
                     int64_t width, int elem_bytes, void* out, int64_t out_stride, int64_t rows_per_group,
-                    int64_t group_stride) {
+                    int64_t group_stride, int out_elem_bytes) {
   if (slots < 0 || width <= 0 || (elem_bytes != 2 && elem_bytes != 4))
     return fail(LP_EINVAL, "bad slots / width / elem_bytes");
+  if (out_elem_bytes != elem_bytes && !(elem_bytes == 4 && out_elem_bytes == 2))
+    return fail(LP_EINVAL, "out_elem_bytes must equal elem_bytes, or be 2 for f32 -> bf16");
   if (rows_per_group <= 0) return fail(LP_EINVAL, "rows_per_group must be positive");
   if (slots == 0) return LP_OK;
   if (src == nullptr || pos == nullptr || out == nullptr) return fail(LP_EINVAL, "null src / pos / out");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (out_elem_bytes != elem_bytes) {
+    if (width % 8 != 0 || src_stride % 4 != 0 || out_stride % 8 != 0 || group_stride % 8 != 0 ||
+        (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+      return fail(LP_EINVAL, "f32 -> bf16 scatter needs width % 8 == 0 and 16-byte aligned rows");
+    ProfScope prof(st, "scatter_rows");
+    const int64_t warps = std::min<int64_t>(slots, 148 * 64);
+    scatter_rows_f32_to_bf16_kernel<<<(unsigned)cdiv(warps * 32, 256), 256, 0, st>>>(
+        reinterpret_cast<const float*>(src), src_stride, pos, slots, width, reinterpret_cast<__nv_bfloat16*>(out),
+        out_stride, rows_per_group, group_stride);
+    LP_LAUNCH_CHECK("scatter_rows_f32_to_bf16_kernel");
+    return LP_OK;
+  }
   const int64_t row_bytes = width * elem_bytes;
   ProfScope prof(st, "scatter_rows");
   const bool vec = row_bytes % 16 == 0 && (src_stride * elem_bytes) % 16 == 0 && (out_stride * elem_bytes) % 16 == 0 &&

@@ -222,6 +222,30 @@ __global__ void scatter_rows_vec_kernel(const uint8_t* __restrict__ src, long lo
   }
 }
 
+// f32 rows -> bf16 rows: one warp per slot row, 8 columns (32 B in, 16 B out) per lane step.
+__global__ void scatter_rows_f32_to_bf16_kernel(const float* __restrict__ src, long long src_stride,
+                                                const int32_t* __restrict__ pos, long long slots, long long width,
+                                                __nv_bfloat16* __restrict__ out, long long out_stride,
+                                                long long rows_per_group, long long group_stride) {
+  const int lane = threadIdx.x & 31;
+  const long long warp_id = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  const long long vec = width / 8;
+  for (long long s = warp_id; s < slots; s += nwarps) {
+    const int p = pos[s];
+    uint4* dst = reinterpret_cast<uint4*>(out + (s / rows_per_group) * group_stride + (s % rows_per_group) * out_stride);
+    if (p >= 0) {
+      const float4* sr = reinterpret_cast<const float4*>(src + (long long)p * src_stride);
+      for (long long v = lane; v < vec; v += 32) {
+        const float4 a = sr[2 * v], b = sr[2 * v + 1];
+        dst[v] = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
+      }
+    } else {
+      for (long long v = lane; v < vec; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
 // Element-wise fallback layout for rows that are not 16-byte multiples (e.g. logps).
 __global__ void scatter_rows_elem_kernel(const uint8_t* __restrict__ src, long long src_stride,
                                          const int32_t* __restrict__ pos, long long slots, long long width,

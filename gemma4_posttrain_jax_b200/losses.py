@@ -19,7 +19,59 @@ import math
 import torch
 
 from . import ops
+from .phase_timer import phase
 from .sharding import VocabMesh, all_gather_stats, all_reduce_sum, vocab_offset
+
+
+# A backward skips the rows whose upstream gradient is exactly zero (they add nothing to dH
+# or dW) when at least this fraction of the rows are zero; the reference's Pallas backward
+# skips all-zero 256-row blocks the same way (pallas/lm_head_logprob_tpuv4.py:185-193).
+_SKIP_ZERO_GRAD_MIN_FRACTION = 0.01
+
+
+def _nonzero_grad_rows(g: torch.Tensor):
+    """Compaction of the rows with g != 0: (idx [m] int32, pos [n] int32, m) or None when dense.
+
+    pos[i] is the compact row of row i, or -1 where g[i] == 0. One device-to-host read of m.
+    """
+    n = g.numel()
+    if n == 0:
+        return None
+    mask = (g != 0).view(1, n)
+    _, _, idx, pos, count = ops.compact(mask)
+    m = int(count.item())
+    if n - m < _SKIP_ZERO_GRAD_MIN_FRACTION * n:
+        return None
+    return idx[:m], pos, m
+
+
+def _gather_rows(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    """src rows at idx (a row gather through lp_scatter_rows); src is [n] or [n, w]."""
+    out = torch.empty((idx.numel(), *src.shape[1:]), dtype=src.dtype, device=src.device)
+    return ops.scatter_rows(src.contiguous(), idx, out)
+
+
+def _backward_rows(embed, H, y, softcap, norm, g, *, vocab_offset, need_dh, need_dw, dh_dtype, dw_dtype,
+                   token_chunk, skip_zero_grad):
+    """shard_backward on the rows with nonzero g; returns (dH rows in compact order or None,
+    dW, pos) where pos maps every row to its dH row (-1 = zero row), or pos None (dense)."""
+    sel = _nonzero_grad_rows(g) if skip_zero_grad else None
+    if sel is None:
+        dH, dW = ops.shard_backward(embed, H, y, softcap, norm, g, vocab_offset=vocab_offset, need_dh=need_dh,
+                                    need_dw=need_dw, dh_dtype=dh_dtype, dw_dtype=dw_dtype, token_chunk=token_chunk)
+        return dH, dW, None
+    idx, pos, m = sel
+    if m == 0:
+        dW = torch.zeros(embed.shape, dtype=dw_dtype, device=embed.device) if need_dw else None
+        dH = torch.zeros((0, H.shape[-1]), dtype=dh_dtype, device=H.device) if need_dh else None
+        return dH, dW, pos
+    Hz = _gather_rows(H.reshape(-1, H.shape[-1]), idx)
+    yz = _gather_rows(y.reshape(-1).to(torch.int32).view(torch.float32), idx).view(torch.int32)
+    gz = _gather_rows(g.reshape(-1).to(torch.float32), idx)
+    nz = torch.stack([_gather_rows(norm[0].contiguous(), idx), _gather_rows(norm[1].contiguous(), idx)])
+    dH, dW = ops.shard_backward(embed, Hz, yz, softcap, nz, gz, vocab_offset=vocab_offset, need_dh=need_dh,
+                                need_dw=need_dw, dh_dtype=dh_dtype, dw_dtype=dw_dtype, token_chunk=token_chunk)
+    return dH, dW, pos
 
 
 def _validate(embed: torch.Tensor, hidden: torch.Tensor, targets: torch.Tensor, vocab_chunk: int, sequence_chunk: int):
@@ -41,12 +93,15 @@ class _CudaTokenLogps(torch.autograd.Function):
     """logp[t] of targets under softcap(H . W^T); grads for W (local shard) and H."""
 
     @staticmethod
-    def forward(ctx, embed, hidden2d, targets1d, softcap, mesh, token_chunk, stats_out):
+    def forward(ctx, embed, hidden2d, targets1d, softcap, mesh, token_chunk, stats_out, dh_reduce_f32=False,
+                skip_zero_grad=True):
         P = mesh.size if mesh is not None else 1
         if P > 1:
             off = vocab_offset(embed.shape[0], mesh)
             stats, _ = ops.shard_forward(embed, hidden2d, targets1d, softcap, vocab_offset=off, want_logp=False)
-            logp, norm = ops.combine(all_gather_stats(stats, mesh))
+            with phase("stats_all_gather"):
+                gathered = all_gather_stats(stats, mesh)
+            logp, norm = ops.combine(gathered)
         else:
             off = 0
             stats, logp = ops.shard_forward(embed, hidden2d, targets1d, softcap, want_logp=True)
@@ -58,6 +113,8 @@ class _CudaTokenLogps(torch.autograd.Function):
         ctx.mesh = mesh
         ctx.offset = off
         ctx.token_chunk = token_chunk
+        ctx.dh_reduce_f32 = dh_reduce_f32
+        ctx.skip_zero_grad = skip_zero_grad
         ctx.mark_non_differentiable(norm)
         return logp
 
@@ -68,10 +125,11 @@ class _CudaTokenLogps(torch.autograd.Function):
         P = mesh.size if mesh is not None else 1
         need_dw, need_dh = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         if not (need_dw or need_dh):
-            return None, None, None, None, None, None, None
-        # Shards sum their dH partials in f32 before the single rounding to the hidden dtype.
-        dh_dtype = torch.float32 if (P > 1 or hidden2d.dtype == torch.float32) else torch.bfloat16
-        dH, dW = ops.shard_backward(
+            return None, None, None, None, None, None, None, None, None
+        # Shards sum their dH partials in the hidden dtype, as the reference's psum of the
+        # bf16 cotangent does (losses.py:253-259 transposed); dh_reduce_f32 sums in f32 instead.
+        dh_dtype = torch.float32 if (P > 1 and ctx.dh_reduce_f32) else torch.bfloat16
+        dH, dW, pos = _backward_rows(
             embed,
             hidden2d,
             targets1d,
@@ -84,12 +142,18 @@ class _CudaTokenLogps(torch.autograd.Function):
             dh_dtype=dh_dtype,
             dw_dtype=embed.dtype if embed.dtype in (torch.bfloat16, torch.float32) else torch.float32,
             token_chunk=ctx.token_chunk,
+            skip_zero_grad=ctx.skip_zero_grad,
         )
         if dH is not None and P > 1:
-            all_reduce_sum(dH, mesh)
-        if dH is not None and dH.dtype != hidden2d.dtype:
+            with phase("dh_all_reduce"):
+                all_reduce_sum(dH, mesh)
+        if dH is not None and pos is not None:
+            # back to one row per token: rows with zero upstream gradient get zero
+            full = torch.empty(hidden2d.shape, dtype=hidden2d.dtype, device=hidden2d.device)
+            dH = ops.scatter_rows(dH, pos, full)
+        elif dH is not None and dH.dtype != hidden2d.dtype:
             dH = dH.to(hidden2d.dtype)
-        return dW, dH, None, None, None, None, None
+        return dW, dH, None, None, None, None, None, None, None
 
 
 def per_token_logps(
@@ -104,6 +168,8 @@ def per_token_logps(
     backend: str = "cuda",
     token_chunk: int | None = None,
     normalization_out: list | None = None,
+    dh_reduce_f32: bool = False,
+    skip_zero_grad: bool = True,
 ) -> torch.Tensor:
     """Selected-token log-probabilities without materialising ``[..., vocab]`` logits.
 
@@ -115,6 +181,9 @@ def per_token_logps(
     so results do not depend on them. ``token_chunk`` bounds the backward's dZ scratch.
     ``normalization_out``, if given, receives the [2, T] (max, sum) statistics of
     ``_vocab_parallel_logps_and_normalization`` (``losses.py:246-260``).
+    ``dh_reduce_f32`` sums the per-shard dH partials in f32 (default: bf16, the reference's
+    precision) before the single rounding to the hidden dtype. ``skip_zero_grad`` runs the
+    backward only on the rows whose upstream gradient is nonzero (results are identical).
     """
     if backend != "cuda":
         if backend in ("jax", "pallas"):
@@ -132,7 +201,8 @@ def per_token_logps(
     y = targets.reshape(-1)
     if y.numel() == 0:
         return torch.zeros(out_shape, dtype=torch.float32, device=hidden.device)
-    logp = _CudaTokenLogps.apply(embed_tokens, h2, y, softcap, mesh, token_chunk, normalization_out)
+    logp = _CudaTokenLogps.apply(embed_tokens, h2, y, softcap, mesh, token_chunk, normalization_out, dh_reduce_f32,
+                                 skip_zero_grad)
     return logp.reshape(out_shape)
 
 
@@ -140,7 +210,8 @@ class _CompletionLogps(torch.autograd.Function):
     """Compacted response-token logprobs; scatters results and dH back to the slot layout."""
 
     @staticmethod
-    def forward(ctx, embed, hidden, completion_ids, completion_mask, prompt_width, softcap, mesh, token_chunk, num_valid):
+    def forward(ctx, embed, hidden, completion_ids, completion_mask, prompt_width, softcap, mesh, token_chunk, num_valid,
+                dh_reduce_f32=False, skip_zero_grad=True):
         B, N = completion_mask.shape
         Hc, yc, idx, pos, count = ops.compact(completion_mask, hidden, completion_ids, row_offset=prompt_width - 1)
         n = int(count.item()) if num_valid is None else int(num_valid)
@@ -150,7 +221,9 @@ class _CompletionLogps(torch.autograd.Function):
         if n > 0:
             if P > 1:
                 stats, _ = ops.shard_forward(embed, Hn, yn, softcap, vocab_offset=off, want_logp=False)
-                logp_c, norm = ops.combine(all_gather_stats(stats, mesh))
+                with phase("stats_all_gather"):
+                    gathered = all_gather_stats(stats, mesh)
+                logp_c, norm = ops.combine(gathered)
             else:
                 stats, logp_c = ops.shard_forward(embed, Hn, yn, softcap, want_logp=True)
                 norm = stats[:2]
@@ -160,35 +233,47 @@ class _CompletionLogps(torch.autograd.Function):
         out = torch.empty((B * N,), dtype=torch.float32, device=hidden.device)
         ops.scatter_rows(logp_c, pos, out)  # out[s] = logp_c[pos[s]] or 0
         ctx.save_for_backward(embed, Hn, yn, norm, idx[:n], pos)
-        ctx.meta = (B, N, n, prompt_width, softcap, mesh, off, token_chunk, tuple(hidden.shape), hidden.dtype)
+        ctx.meta = (B, N, n, prompt_width, softcap, mesh, off, token_chunk, tuple(hidden.shape), hidden.dtype,
+                    dh_reduce_f32, skip_zero_grad)
         return out.reshape(B, N)
 
     @staticmethod
     def backward(ctx, g):
         embed, Hn, yn, norm, idx_n, pos = ctx.saved_tensors
-        B, N, n, prompt_width, softcap, mesh, off, token_chunk, hshape, hdtype = ctx.meta
+        B, N, n, prompt_width, softcap, mesh, off, token_chunk, hshape, hdtype, dh_reduce_f32, skip_zero_grad = ctx.meta
         P = mesh.size if mesh is not None else 1
         need_dw, need_dh = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         dW = dhidden = None
         if n > 0 and (need_dw or need_dh):
             gc = torch.empty((n,), dtype=torch.float32, device=g.device)
             ops.scatter_rows(g.reshape(-1).to(torch.float32).contiguous(), idx_n, gc)  # gc[i] = g[idx[i]]
-            dHc, dW = ops.shard_backward(
+            dHc, dW, posz = _backward_rows(
                 embed, Hn, yn, softcap, norm, gc, vocab_offset=off, need_dh=need_dh, need_dw=need_dw,
-                dh_dtype=torch.float32 if P > 1 else torch.bfloat16, dw_dtype=embed.dtype, token_chunk=token_chunk,
+                dh_dtype=torch.float32 if (P > 1 and dh_reduce_f32) else torch.bfloat16, dw_dtype=embed.dtype,
+                token_chunk=token_chunk, skip_zero_grad=skip_zero_grad,
             )
+            if posz is not None:
+                # slot -> compact row -> nonzero-gradient row (or -1)
+                pos = torch.where(pos >= 0, posz[pos.clamp(min=0).long()], torch.full_like(pos, -1))
             if dHc is not None:
                 if P > 1:
-                    all_reduce_sum(dHc, mesh)
-                    dHc = dHc.to(torch.bfloat16)
-                dhidden = torch.zeros(hshape, dtype=hdtype, device=g.device)
-                # response slice hidden[:, P-1 : P-1+N] receives dHc at valid slots, 0 elsewhere
+                    with phase("dh_all_reduce"):
+                        all_reduce_sum(dHc, mesh)
+                with phase("dh_zero_fill"):
+                    # rows outside the response slice get 0; the scatter writes every slice row
+                    dhidden = torch.empty(hshape, dtype=hdtype, device=g.device)
+                    if prompt_width > 1:
+                        dhidden[:, : prompt_width - 1].zero_()
+                    if prompt_width - 1 + N < hshape[1]:
+                        dhidden[:, prompt_width - 1 + N :].zero_()
+                # response slice hidden[:, P-1 : P-1+N] receives dHc at valid slots (summed f32
+                # partials are rounded to bf16 by the scatter), 0 elsewhere
                 ops.scatter_rows(dHc, pos, dhidden[:, prompt_width - 1 : prompt_width - 1 + N])
         if need_dw and dW is None:
             dW = torch.zeros_like(embed)
         if need_dh and dhidden is None:
             dhidden = torch.zeros(hshape, dtype=hdtype, device=g.device)
-        return dW, dhidden, None, None, None, None, None, None, None
+        return dW, dhidden, None, None, None, None, None, None, None, None, None
 
 
 def completion_logps(
@@ -202,6 +287,8 @@ def completion_logps(
     mesh: VocabMesh | None = None,
     token_chunk: int | None = None,
     num_valid: int | None = None,
+    dh_reduce_f32: bool = False,
+    skip_zero_grad: bool = True,
 ) -> torch.Tensor:
     """Response-token logprobs of ``trainer_completion_logps`` (``losses.py:667-682``).
 
@@ -209,7 +296,7 @@ def completion_logps(
     by position ``prompt_width + j - 1``. Only ``completion_mask`` slots are computed
     (compaction); invalid slots return 0, as ``where(completion_mask, logps, 0)`` does.
     ``num_valid`` (the mask's popcount, when the caller knows it on the host) avoids one
-    device-to-host read.
+    device-to-host read. ``dh_reduce_f32``, ``skip_zero_grad``: see ``per_token_logps``.
     """
     if hidden.ndim != 3 or completion_ids.ndim != 2 or completion_mask.shape != completion_ids.shape:
         raise ValueError("hidden must be [B, S, d] and completion ids / mask [B, N]")
@@ -217,7 +304,8 @@ def completion_logps(
         raise ValueError("prompt_width and completion width do not fit the hidden sequence")
     _validate_softcap(softcap)
     return _CompletionLogps.apply(
-        embed_tokens, hidden, completion_ids, completion_mask, int(prompt_width), softcap, mesh, token_chunk, num_valid
+        embed_tokens, hidden, completion_ids, completion_mask, int(prompt_width), softcap, mesh, token_chunk, num_valid,
+        dh_reduce_f32, skip_zero_grad,
     )
 
 

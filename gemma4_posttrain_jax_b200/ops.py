@@ -226,13 +226,14 @@ def scatter_rows(src: torch.Tensor, pos: torch.Tensor, out: torch.Tensor) -> tor
 
     ``out`` is [slots] / [slots, width] or a strided [B, N, width] view (slot s = b * N + j),
     e.g. the response slice of a [B, S, d] gradient. Also serves as a row gather
-    (``pos`` = source row of every output row).
+    (``pos`` = source row of every output row). f32 ``src`` may be written to a bf16 ``out``.
     """
     dev = _require_cuda(src, pos, out)
     lib = _lib.load()
-    if src.dtype != out.dtype or src.dtype not in (torch.bfloat16, torch.float32):
-        raise ValueError("src / out must share a bf16 or f32 dtype")
-    s2 = src.reshape(src.shape[0], -1) if src.ndim > 1 else src.reshape(-1, 1)
+    if src.dtype not in (torch.bfloat16, torch.float32) or not (
+        src.dtype == out.dtype or (src.dtype == torch.float32 and out.dtype == torch.bfloat16)
+    ):
+        raise ValueError("src / out must share a bf16 or f32 dtype, or be f32 -> bf16")
     if out.ndim == 3:
         B, N, width = out.shape
         rows_per_group, group_stride, row_stride = N, int(out.stride(0)), int(out.stride(1))
@@ -245,15 +246,19 @@ def scatter_rows(src: torch.Tensor, pos: torch.Tensor, out: torch.Tensor) -> tor
         B, (N, width) = 1, o2.shape
         rows_per_group, row_stride = N, int(o2.stride(0))
         group_stride = N * row_stride
+    s2 = src.reshape(src.shape[0], width)
     slots = B * N
     if s2.stride(-1) != 1:
         s2 = s2.contiguous()
     if pos.numel() != slots or s2.shape[1] != width:
         raise ValueError("pos / src / out shapes disagree")
     p = pos.to(torch.int32).contiguous()
+    # an empty src is never read (every pos is -1); any valid pointer stands in for it
+    src_ptr = _ptr(s2) if s2.shape[0] > 0 else _ptr(out)
+    src_ld = int(s2.stride(0)) if s2.shape[0] > 0 else width
     rc = lib.lp_scatter_rows(
-        _stream(dev), _ptr(s2), int(s2.stride(0)), _ptr(p), slots, width, src.element_size(), _ptr(out), row_stride,
-        rows_per_group, group_stride,
+        _stream(dev), src_ptr, src_ld, _ptr(p), slots, width, src.element_size(), _ptr(out), row_stride,
+        rows_per_group, group_stride, out.element_size(),
     )
     _lib.check(rc, "lp_scatter_rows")
     return out

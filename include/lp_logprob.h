@@ -181,11 +181,12 @@ LP_API int lp_compact(void* stream, const uint8_t* mask, int64_t B, int64_t N, c
  *   row(s) = out + (s / rows_per_group) * group_stride + (s % rows_per_group) * out_stride
  * so a strided [B, N, width] view (rows_per_group = N) such as the response slice of a
  * [B, S, d] gradient is written in place. With pos = a list of source rows it is a row
- * gather. elem_bytes is 2 (bf16) or 4 (f32); strides are in elements.
+ * gather. elem_bytes is 2 (bf16) or 4 (f32) for src; out_elem_bytes equals it, or is 2
+ * with f32 src (rows converted to bf16 on the way). Strides are in elements.
  */
 LP_API int lp_scatter_rows(void* stream, const void* src, int64_t src_stride, const int32_t* pos, int64_t slots,
                     int64_t width, int elem_bytes, void* out, int64_t out_stride, int64_t rows_per_group,
-                    int64_t group_stride);
+                    int64_t group_stride, int out_elem_bytes);
 
 /*
  * Test hook of the tensor-core core (no reference counterpart): D[M, N] = A . B^T in f32,

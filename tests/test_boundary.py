@@ -82,8 +82,9 @@ def test_small_entry_points_validate(lib):
     P = ctypes.c_void_p
     fake = P(16)
     _einval(lib.lp_combine(None, fake, 0, 5, fake, fake), lib, "bad P")
-    _einval(lib.lp_scatter_rows(None, fake, 1, fake, 4, 1, 3, fake, 1, 4, 4), lib, "elem_bytes")
-    _einval(lib.lp_scatter_rows(None, fake, 1, fake, 4, 1, 4, fake, 1, 0, 4), lib, "rows_per_group")
+    _einval(lib.lp_scatter_rows(None, fake, 1, fake, 4, 1, 3, fake, 1, 4, 4, 3), lib, "elem_bytes")
+    _einval(lib.lp_scatter_rows(None, fake, 1, fake, 4, 1, 2, fake, 1, 4, 4, 4), lib, "out_elem_bytes")
+    _einval(lib.lp_scatter_rows(None, fake, 1, fake, 4, 1, 4, fake, 1, 0, 4, 4), lib, "rows_per_group")
     _einval(lib.lp_compact(None, None, 2, 3, None, 0, 0, 0, 0, None, None, None, fake, fake, fake, fake, 1024), lib,
             "null mask")
     _einval(lib.lp_gemm_bf16(None, fake, 0, 8, 8, 0, fake, 8, 8, 0, fake, 8), lib, "sizes")

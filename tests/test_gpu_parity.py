@@ -265,6 +265,13 @@ def test_compaction_gather_and_scatter(cuda_device):
     exp[b, j] = hidden[b, j + pw - 1]
     np.testing.assert_array_equal(o[:, pw - 1: pw - 1 + N], exp)
     assert (o[:, : pw - 1] == 7.0).all() and (o[:, pw - 1 + N:] == 7.0).all()
+    # f32 rows scattered into a bf16 slice are rounded on the way
+    src32 = torch.from_numpy(rng.normal(size=(n, d)).astype(np.float32)).to(cuda_device)
+    out16 = torch.full((B, S, d), 7.0, dtype=torch.bfloat16, device=cuda_device)
+    ops.scatter_rows(src32, pos, out16[:, pw - 1: pw - 1 + N])
+    exp16 = torch.zeros((B, N, d), dtype=torch.bfloat16)
+    exp16[torch.from_numpy(b), torch.from_numpy(j)] = src32.cpu().to(torch.bfloat16)
+    assert torch.equal(out16[:, pw - 1: pw - 1 + N].cpu(), exp16)
 
 
 def test_completion_logps_autograd_matches_oracle(cuda_device):
@@ -348,3 +355,51 @@ def test_config1_shape_fwd_bwd(cuda_device, cta_group):
     assert np.abs(logp.cpu().numpy() - lp_ref).max() <= LOGP_ATOL
     assert rel_l2(dH.cpu().numpy(), dH_ref) <= GRAD_REL_L2
     assert rel_l2(dW.cpu().numpy(), dW_ref) <= GRAD_REL_L2
+
+
+def test_zero_gradient_rows_are_skipped_without_changing_results(cuda_device):
+    """The backward runs only on rows with nonzero upstream gradient; dH rows of the others
+    are exactly zero and every other result equals the dense backward's up to f32 order."""
+    from gemma4_posttrain_jax_b200.losses import completion_logps, per_token_logps
+
+    rng = np.random.default_rng(29)
+    T, d, V = 700, 96, 3000
+    w = orc.bf16_round(rng.normal(size=(V, d)) * 0.3)
+    h = orc.bf16_round(rng.normal(size=(T, d)))
+    y = rng.integers(0, V, size=T).astype(np.int32)
+    g = rng.normal(size=T).astype(np.float32) * (rng.random(T) < 0.6)
+    grads = []
+    for skip in (True, False):
+        W = to_bf16(w, cuda_device).requires_grad_(True)
+        H = to_bf16(h, cuda_device).requires_grad_(True)
+        lp = per_token_logps(W, H, torch.from_numpy(y).to(cuda_device), softcap=30.0, skip_zero_grad=skip)
+        (lp * torch.from_numpy(g).to(cuda_device)).sum().backward()
+        grads.append((W.grad.float().cpu().numpy(), H.grad.float().cpu().numpy()))
+    # dW / dH come back in bf16: a different f32 summation order flips a few roundings
+    assert rel_l2(grads[0][0], grads[1][0]) < 1e-3
+    assert rel_l2(grads[0][1], grads[1][1]) < 1e-3
+    assert (grads[0][1][g == 0] == 0).all()
+    _, dW_ref, dH_ref = orc.logps_grads_f64(w, h, y, g, 30.0)
+    assert rel_l2(grads[0][0], dW_ref) <= GRAD_REL_L2 and rel_l2(grads[0][1], dH_ref) <= GRAD_REL_L2
+    # all-zero upstream gradient: zero dW and dH
+    W = to_bf16(w, cuda_device).requires_grad_(True)
+    H = to_bf16(h, cuda_device).requires_grad_(True)
+    lp = per_token_logps(W, H, torch.from_numpy(y).to(cuda_device), softcap=30.0)
+    (lp * 0.0).sum().backward()
+    assert (W.grad == 0).all() and (H.grad == 0).all()
+    # GRPO caller with zero-advantage sequences
+    B, Pw, N = 4, 3, 50
+    hid = orc.bf16_round(rng.normal(size=(B, Pw + N, d)))
+    ids = rng.integers(0, V, size=(B, N)).astype(np.int32)
+    mask = np.arange(N)[None, :] < np.array([50, 20, 0, 33])[:, None]
+    adv = np.array([[0.7], [0.0], [1.0], [-0.4]], np.float32) * (rng.random((B, N)) < 0.8)
+    outs = []
+    for skip in (True, False):
+        W = to_bf16(w, cuda_device).requires_grad_(True)
+        Hd = to_bf16(hid, cuda_device).requires_grad_(True)
+        out = completion_logps(W, Hd, torch.from_numpy(ids).to(cuda_device), torch.from_numpy(mask).to(cuda_device),
+                               prompt_width=Pw, softcap=30.0, skip_zero_grad=skip)
+        (out * torch.from_numpy(adv).to(cuda_device)).sum().backward()
+        outs.append((W.grad.float().cpu().numpy(), Hd.grad.float().cpu().numpy()))
+    assert rel_l2(outs[0][0], outs[1][0]) < 1e-3
+    assert rel_l2(outs[0][1], outs[1][1]) < 1e-3
