@@ -42,6 +42,14 @@ SOFTCAP = 30.0
 SEED = 0
 METRIC = "logprob fwd+bwd tokens/s @V=262144,d=2048 (GRPO response tokens, vocab-sharded)"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) per launch of each GEMM on this workload at N=1, from one ncu
+# capture (profiles/dram_traffic_grpo_config2_1gpu.md); backward launches: an 8192-row chunk.
+NCU_TRAFFIC_PER_LAUNCH_N1 = {
+    "fwd_lse_gemm": 22.70e9,
+    "bwd_dz_gemm": 5.73e9,
+    "bwd_dh_gemm": 20.40e9,
+    "bwd_dw_gemm": 11.58e9,
+}
 
 
 def parse_args():
@@ -414,7 +422,9 @@ def main():
             "peak": peaks["bf16_tflops_sustained"],
             "unit": "TFLOP/s",
             "frac": achieved / peaks["bf16_tflops_sustained"],
-            "traffic": None,
+            "traffic": (NCU_TRAFFIC_PER_LAUNCH_N1.get(dom)
+                        if world == 1 and args.batch == B and args.softcap == SOFTCAP else None),
+            "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
             "peak_source": f"bf16_tflops_sustained ({peak_src}); kernel runs inside a long step",
             "flop_per_launch": flop_per_launch,
         }
