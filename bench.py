@@ -52,6 +52,10 @@ NCU_TRAFFIC_PER_LAUNCH_N1 = {
 }
 
 
+# Dense-token BASELINE configs: (tokens, hidden, frozen head, extra forward-only pass).
+DENSE_CONFIGS = {1: (256, 2048, False, False), 3: (65536, 2560, False, True), 4: (32768, 3840, True, False)}
+
+
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -60,6 +64,11 @@ def parse_args():
     p.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
     p.add_argument("--softcap", type=float, default=SOFTCAP, help="<= 0 disables the softcap")
     p.add_argument("--batch", type=int, default=B, help="sequences (default: config 2's 128)")
+    p.add_argument("--config", type=int, default=2, choices=(1, 2, 3, 4),
+                   help="BASELINE config: 2 = GRPO response tokens (the metric's workload, default); "
+                        "1 = T=256 dense; 3 = T=65536, d=2560 + forward-only pass of a perturbed head; "
+                        "4 = T=32768, d=3840, frozen head (forward + dH)")
+    p.add_argument("--tokens", type=int, default=0, help="override T of configs 1 / 3 / 4")
     p.add_argument("--token-chunk", type=int, default=0, help="backward token chunk (0 = library default)")
     p.add_argument("--cta-group", type=int, default=0, choices=(0, 1, 2),
                    help="tensor-core CTA group of the GEMMs (0 = library default, the CTA pair)")
@@ -287,30 +296,74 @@ def main():
         mesh = VocabMesh(None)
 
     softcap = args.softcap if args.softcap > 0 else None
-    prompt_len, resp_len, mask_np, ids_np, g_np = make_batch(args.batch)
-    n_valid = int(mask_np.sum())
-    # rows the backward computes: valid tokens with nonzero dlogp (zero-gradient rows are
-    # skipped by the library, as the reference's Pallas backward skips all-zero blocks)
-    n_bwd = int((g_np[mask_np] != 0).sum())
-    vs = V // world
-
-    # inputs: the same seeded draws on every rank; each rank keeps its W row block
-    gen = torch.Generator(device=dev).manual_seed(SEED + 1)
-    W_full = (torch.randn((V, D), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
-    W = W_full[rank * vs : (rank + 1) * vs].clone().requires_grad_(True)
-    del W_full
-    gen_h = torch.Generator(device=dev).manual_seed(SEED + 2)
-    H = torch.randn((args.batch, RESP, D), generator=gen_h, device=dev).to(torch.bfloat16).requires_grad_(True)
-    ids = torch.from_numpy(ids_np).to(dev)
-    mask = torch.from_numpy(mask_np).to(dev)
-    g = torch.from_numpy(g_np).to(dev)
     chunk = args.token_chunk or None
+    from gemma4_posttrain_jax_b200.losses import per_token_logps
 
-    def step(Hx, idsx, maskx, gx):
-        lp = completion_logps(W, Hx, idsx, maskx, prompt_width=1, softcap=softcap, mesh=mesh, token_chunk=chunk,
-                              num_valid=n_valid)
-        dW, dH = torch.autograd.grad(lp, (W, Hx), gx)
-        return lp, dW, dH
+    if args.config == 2:
+        d_model = D
+        prompt_len, resp_len, mask_np, ids_np, g_np = make_batch(args.batch)
+        n_valid = int(mask_np.sum())
+        # rows the backward computes: valid tokens with nonzero dlogp (zero-gradient rows are
+        # skipped by the library, as the reference's Pallas backward skips all-zero blocks)
+        n_bwd = int((g_np[mask_np] != 0).sum())
+        vs = V // world
+        # inputs: the same seeded draws on every rank; each rank keeps its W row block
+        gen = torch.Generator(device=dev).manual_seed(SEED + 1)
+        W_full = (torch.randn((V, D), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        W = W_full[rank * vs : (rank + 1) * vs].clone().requires_grad_(True)
+        del W_full
+        gen_h = torch.Generator(device=dev).manual_seed(SEED + 2)
+        H = torch.randn((args.batch, RESP, D), generator=gen_h, device=dev).to(torch.bfloat16).requires_grad_(True)
+        ids = torch.from_numpy(ids_np).to(dev)
+        mask = torch.from_numpy(mask_np).to(dev)
+        g = torch.from_numpy(g_np).to(dev)
+        inputs = [H.detach(), ids, mask, g]
+        fwd_launch_flops = 2.0 * n_valid * D * vs
+        bwd_launch_flops = {"bwd_dz_gemm": 2.0 * n_bwd * D * vs, "bwd_dh_gemm": 2.0 * n_bwd * D * vs,
+                            "bwd_dw_gemm": 2.0 * n_bwd * D * vs}
+        total_flops_needed = 2.0 * n_valid * D * V + 6.0 * n_bwd * D * V
+        dense_flops = 8.0 * n_valid * D * V
+
+        def step(Hx, idsx, maskx, gx):
+            Hx = Hx.detach().requires_grad_(True)
+            lp = completion_logps(W, Hx, idsx, maskx, prompt_width=1, softcap=softcap, mesh=mesh, token_chunk=chunk,
+                                  num_valid=n_valid)
+            dW, dH = torch.autograd.grad(lp, (W, Hx), gx)
+            return lp, dW, dH
+    else:
+        T_cfg, d_model, frozen, second_pass = DENSE_CONFIGS[args.config]
+        T_cfg = args.tokens or T_cfg
+        n_valid = n_bwd = T_cfg
+        vs = V // world
+        gen = torch.Generator(device=dev).manual_seed(SEED + 1)
+        W_full = (torch.randn((V, d_model), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        W = W_full[rank * vs : (rank + 1) * vs].clone().requires_grad_(not frozen)
+        W2 = None
+        if second_pass:  # old / reference policy head: W + N(0, 1e-4)
+            W2 = (W.detach().float() + torch.randn(W.shape, generator=gen, device=dev) * 1e-4).to(torch.bfloat16)
+        del W_full
+        gen_h = torch.Generator(device=dev).manual_seed(SEED + 2)
+        Hd = torch.randn((T_cfg, d_model), generator=gen_h, device=dev).to(torch.bfloat16)
+        Yd = torch.randint(0, V, (T_cfg,), generator=gen_h, device=dev, dtype=torch.int32)
+        Gd = torch.randn((T_cfg,), generator=gen_h, device=dev)
+        inputs = [Hd, Yd, Gd]
+        fwd_launch_flops = 2.0 * T_cfg * d_model * vs
+        bwd_launch_flops = {"bwd_dz_gemm": 2.0 * T_cfg * d_model * vs, "bwd_dh_gemm": 2.0 * T_cfg * d_model * vs}
+        if not frozen:
+            bwd_launch_flops["bwd_dw_gemm"] = 2.0 * T_cfg * d_model * vs
+        total_flops_needed = (2.0 * (2 if second_pass else 1) + (4.0 if frozen else 6.0)) * T_cfg * d_model * V
+        dense_flops = total_flops_needed
+
+        def step(Hx, Yx, Gx):
+            Hx = Hx.detach().requires_grad_(True)
+            lp = per_token_logps(W, Hx, Yx, softcap=softcap, mesh=mesh, token_chunk=chunk)
+            wrt = (Hx,) if frozen else (W, Hx)
+            grads = torch.autograd.grad(lp, wrt, Gx)
+            if W2 is not None:
+                with torch.no_grad():
+                    lp2 = per_token_logps(W2, Hx.detach(), Yx, softcap=softcap, mesh=mesh)
+                return lp, lp2, grads
+            return lp, grads
 
     def barrier():
         if world > 1:
@@ -325,7 +378,7 @@ def main():
 
     # ---------------------------------------------------------------- device-resident timing
     for _ in range(args.warmup):
-        step(H, ids, mask, g)
+        step(*inputs)
     torch.cuda.synchronize()
     assert _lib.device_error(local) == 0, "device-side error during warm-up"
     barrier()
@@ -339,7 +392,7 @@ def main():
     with ClockSampler(list(range(world))) as clocks:
         start.record()
         for _ in range(args.steps):
-            step(H, ids, mask, g)
+            step(*inputs)
         stop.record()
         torch.cuda.synchronize()
     barrier()
@@ -357,23 +410,18 @@ def main():
     # ---------------------------------------------------------------- end-to-end (host buffers)
     e2e = None
     if not args.no_e2e:
-        H_host = H.detach().cpu().pin_memory()
-        ids_host = torch.from_numpy(ids_np).pin_memory()
-        mask_host = torch.from_numpy(mask_np).pin_memory()
-        g_host = torch.from_numpy(g_np).pin_memory()
-        out_host = torch.empty((args.batch, RESP), dtype=torch.float32).pin_memory()
-        H_dev = torch.empty_like(H.detach())
-        ids_dev, mask_dev, g_dev = torch.empty_like(ids), torch.empty_like(mask), torch.empty_like(g)
-        h2d = H_host.nbytes + ids_host.nbytes + mask_host.nbytes + g_host.nbytes
+        hosts = [x.detach().cpu().pin_memory() for x in inputs]
+        devs = [torch.empty_like(x) for x in inputs]
+        out_shape = (args.batch, RESP) if args.config == 2 else (n_valid,)
+        out_host = torch.empty(out_shape, dtype=torch.float32).pin_memory()
+        h2d = sum(x.nbytes for x in hosts)
         d2h = out_host.nbytes
 
         def e2e_step():
-            H_dev.copy_(H_host, non_blocking=True)
-            ids_dev.copy_(ids_host, non_blocking=True)
-            mask_dev.copy_(mask_host, non_blocking=True)
-            g_dev.copy_(g_host, non_blocking=True)
-            lp, _, _ = step(H_dev.detach().requires_grad_(True), ids_dev, mask_dev, g_dev)
-            out_host.copy_(lp.detach(), non_blocking=True)
+            for hx, dx in zip(hosts, devs):
+                dx.copy_(hx, non_blocking=True)
+            out = step(*devs)
+            out_host.copy_(out[0].detach(), non_blocking=True)
 
         for _ in range(args.warmup):
             e2e_step()
@@ -393,12 +441,8 @@ def main():
 
     # ---------------------------------------------------------------- roofline of the dominant kernel
     peaks, peak_src = load_peaks()
-    flops_per_step = {
-        "fwd_lse_gemm": 2.0 * n_valid * D * vs,
-        "bwd_dz_gemm": 2.0 * n_bwd * D * vs,
-        "bwd_dh_gemm": 2.0 * n_bwd * D * vs,
-        "bwd_dw_gemm": 2.0 * n_bwd * D * vs,
-    }
+    n_fwd_passes = 2 if (args.config == 3) else 1
+    flops_per_step = {"fwd_lse_gemm": fwd_launch_flops * n_fwd_passes, **bwd_launch_flops}
     kernels = {}
     for name, (tot_ms, cnt) in prof.items():
         per_launch = tot_ms / max(cnt, 1)
@@ -423,18 +467,17 @@ def main():
             "unit": "TFLOP/s",
             "frac": achieved / peaks["bf16_tflops_sustained"],
             "traffic": (NCU_TRAFFIC_PER_LAUNCH_N1.get(dom)
-                        if world == 1 and args.batch == B and args.softcap == SOFTCAP else None),
+                        if world == 1 and args.config == 2 and args.batch == B and args.softcap == SOFTCAP else None),
             "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
             "peak_source": f"bf16_tflops_sustained ({peak_src}); kernel runs inside a long step",
             "flop_per_launch": flop_per_launch,
         }
-    total_flops = 2.0 * n_valid * D * V + 6.0 * n_bwd * D * V  # the GEMM work one step needs
-    step_tflops = total_flops / (ms / 1e3) / 1e12
-    dense_equiv_tflops = 8.0 * n_valid * D * V / (ms / 1e3) / 1e12  # the 8*T*d*V roofline's count
+    step_tflops = total_flops_needed / (ms / 1e3) / 1e12  # the GEMM work one step needs
+    dense_equiv_tflops = dense_flops / (ms / 1e3) / 1e12  # the 8*T*d*V roofline's count (config 2)
 
     # ---------------------------------------------------------------- CPU baseline (rank 0, N = 1)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == 2:
         Wf = W.detach().float().cpu().numpy()
         Hf = H.detach().float().cpu().numpy()
         sample = 64
@@ -447,8 +490,17 @@ def main():
                f"({t:.1f} s), numpy float32 restatement of losses.py:72-147 + recompute backward"}
 
     if rank == 0:
+        metric = METRIC if args.config == 2 else (
+            f"logprob tokens/s @V=262144,d={d_model} (BASELINE config {args.config}, vocab-sharded)")
+        cfg = config_dict(args.batch, n_valid, world, args.softcap) if args.config == 2 else {
+            "workload": f"BASELINE config {args.config}: "
+            + {1: "dense fwd+bwd", 3: "dense fwd+bwd + forward-only pass of W + N(0,1e-4)",
+               4: "dense fwd + dH, frozen head"}[args.config],
+            "tokens": n_valid, "hidden": d_model, "vocab": V, "vocab_per_gpu": vs,
+            "softcap": args.softcap if args.softcap > 0 else None, "parallelism": f"vocab{world}",
+            "l2": "no flush: W shard exceeds the 126 MB L2"}
         line = {
-            "metric": METRIC,
+            "metric": metric,
             "value": value,
             "unit": "tokens/s",
             "n_gpus": world,
@@ -460,7 +512,7 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) hidden, N(0,0.02) W, uniform targets)",
-            "config": config_dict(args.batch, n_valid, world, args.softcap),
+            "config": cfg,
             "clocks": clock_summary,
             "e2e": e2e,
             "gpu_launches": int(launches),

@@ -403,3 +403,36 @@ def test_zero_gradient_rows_are_skipped_without_changing_results(cuda_device):
         outs.append((W.grad.float().cpu().numpy(), Hd.grad.float().cpu().numpy()))
     assert rel_l2(outs[0][0], outs[1][0]) < 1e-3
     assert rel_l2(outs[0][1], outs[1][1]) < 1e-3
+
+
+@pytest.mark.parametrize("d,frozen_head", [(2560, False), (3840, True)])
+def test_config3_and_config4_hidden_sizes(cuda_device, d, frozen_head):
+    """BASELINE config 3 (d=2560, fwd+bwd plus a forward-only pass over W + N(0, 1e-4)) and
+    config 4 (d=3840, frozen head: forward + dH only) at the full V=262144, on 256 tokens."""
+    from gemma4_posttrain_jax_b200 import ops
+
+    T, V = 256, 262144
+    gen = torch.Generator(device="cpu").manual_seed(d)
+    h = torch.randn((T, d), generator=gen).to(torch.bfloat16)
+    w = (torch.randn((V, d), generator=gen) * 0.02).to(torch.bfloat16)
+    y = torch.randint(0, V, (T,), generator=gen, dtype=torch.int32)
+    g = torch.randn((T,), generator=gen)
+    W, H, Y, G = w.to(cuda_device), h.to(cuda_device), y.to(cuda_device), g.to(cuda_device)
+    stats, logp = ops.shard_forward(W, H, Y, 30.0)
+    dH, dW = ops.shard_backward(W, H, Y, 30.0, stats[:2], G, need_dw=not frozen_head, dh_dtype=torch.float32)
+    torch.cuda.synchronize()
+    wn, hn = w.float().numpy(), h.float().numpy()
+    lp_ref, dW_ref, dH_ref = orc.fwd_bwd_f32(wn, hn, y.numpy(), g.numpy(), softcap=30.0, vocab_chunk=8192,
+                                            sequence_chunk=128)
+    assert np.abs(logp.cpu().numpy() - lp_ref).max() <= LOGP_ATOL
+    assert rel_l2(dH.cpu().numpy(), dH_ref) <= GRAD_REL_L2
+    if frozen_head:
+        assert dW is None
+    else:
+        assert rel_l2(dW.float().cpu().numpy(), dW_ref) <= GRAD_REL_L2
+        # the second, forward-only pass of config 3 over a perturbed head (old / reference policy)
+        w2 = (w.float() + torch.randn((V, d), generator=gen) * 1e-4).to(torch.bfloat16)
+        _, logp2 = ops.shard_forward(w2.to(cuda_device), H, Y, 30.0)
+        lp2_ref = orc.single_partition_logps(w2.float().numpy(), hn, y.numpy(), softcap=30.0, vocab_chunk=8192,
+                                             sequence_chunk=128)
+        assert np.abs(logp2.cpu().numpy() - lp2_ref).max() <= LOGP_ATOL
