@@ -36,6 +36,8 @@ _SIG = {
     "lp_set_cta_group": (ctypes.c_int, [ctypes.c_int]),
     "lp_get_cta_group": (ctypes.c_int, []),
     "lp_device_pairs": (ctypes.c_int, []),
+    "lp_debug_enable": (ctypes.c_int, [ctypes.c_int]),
+    "lp_debug_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_ulonglong)]),
     "lp_profile_enable": (ctypes.c_int, [ctypes.c_int]),
     "lp_profile_read": (
         ctypes.c_int,
@@ -140,6 +142,22 @@ def set_cta_group(cg: int) -> None:
 
 def cta_group() -> int:
     return int(load().lp_get_cta_group())
+
+
+DEBUG_KINDS = ("fwd", "dz", "dh", "dw", "other")
+DEBUG_FIELDS = ("prod_wait", "mma_wait_load", "mma_wait_acc", "epi_wait", "mma_cycles", "kblocks", "epi_busy", "tiles")
+
+
+def debug_enable(on: bool = True) -> None:
+    """Zero (and switch on / off) the GEMM pipeline counters of the current device."""
+    check(load().lp_debug_enable(1 if on else 0), "lp_debug_enable")
+
+
+def debug_read() -> dict[str, dict[str, int]]:
+    """{gemm kind: {counter: total over CTAs}} of the counters since debug_enable."""
+    out = (ctypes.c_ulonglong * 40)()
+    check(load().lp_debug_read(out), "lp_debug_read")
+    return {k: {f: int(out[i * 8 + j]) for j, f in enumerate(DEBUG_FIELDS)} for i, k in enumerate(DEBUG_KINDS)}
 
 
 def launch_count() -> int:

@@ -94,6 +94,25 @@ constexpr int kMaxDevices = 64;
 // 128x256 tiles. By default each GEMM uses the group that measured faster for it;
 // LP_B200_CTA_GROUP=1|2 or lp_set_cta_group(1|2) forces one group for every GEMM.
 // 0 = per-GEMM default (below); 1 / 2 = force every GEMM to that CTA group.
+// Optional pipeline counters of the GEMM kernels (a tuning aid): one 8-counter block per CTA
+// and per GEMM kind, allocated on the first lp_debug_enable(1) of a device.
+constexpr int kDbgKinds = 5;  // fwd, dz, dh, dw, other
+std::atomic<bool> g_dbg_on{false};
+unsigned long long* g_dbg_buf[kMaxDevices] = {};
+int dbg_kind(const char* tag) {
+  if (!strcmp(tag, "fwd_lse_gemm")) return 0;
+  if (!strcmp(tag, "bwd_dz_gemm")) return 1;
+  if (!strcmp(tag, "bwd_dh_gemm")) return 2;
+  if (!strcmp(tag, "bwd_dw_gemm")) return 3;
+  return 4;
+}
+unsigned long long* dbg_ptr(const char* tag) {
+  if (!g_dbg_on.load()) return nullptr;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || g_dbg_buf[dev] == nullptr) return nullptr;
+  return g_dbg_buf[dev] + (size_t)dbg_kind(tag) * 256 * 8;
+}
+
 std::atomic<int> g_cg{-1};
 
 int forced_cta_group() {
@@ -215,10 +234,6 @@ int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize
 int map_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems, uint32_t bi,
              uint32_t bo, const char* what) {
   return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, outer, ld_elems * 2, bi, bo, what);
-}
-int map_f32(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems, uint32_t bi,
-            uint32_t bo, const char* what) {
-  return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, inner, outer, ld_elems * 4, bi, bo, what);
 }
 
 // Epilogue store targets: one 32-row x 64-byte box per warp and piece, 64-byte swizzle
@@ -371,9 +386,11 @@ int launch_gemm_cg(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, 
     configured[dev] = true;
   }
   const int grid = CG * std::max(1, std::min(p.s.num_units, workers(di, CG)));
+  GemmParams pp = p;
+  pp.dbg = dbg_ptr(tag);
   ProfScope prof(st, tag);
   if constexpr (CG == 1) {
-    kern<<<grid, NUM_THREADS, smem, st>>>(a, b, o, p);
+    kern<<<grid, NUM_THREADS, smem, st>>>(a, b, o, pp);
   } else {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
@@ -387,7 +404,7 @@ int launch_gemm_cg(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    LP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, b, o, p));
+    LP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, b, o, pp));
   }
   LP_LAUNCH_CHECK("tc_gemm_kernel");
   return LP_OK;
@@ -457,6 +474,35 @@ int lp_version(void) { return 100; }
 const char* lp_last_error(void) { return g_last_error.c_str(); }
 
 long long lp_launch_count(void) { return g_launches.load(); }
+
+int lp_debug_enable(int on) {
+  int dev = 0;
+  LP_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(LP_EINVAL, "device ordinal out of range");
+  if (on && g_dbg_buf[dev] == nullptr) {
+    LP_CUDA_TRY(cudaMalloc(&g_dbg_buf[dev], (size_t)kDbgKinds * 256 * 8 * sizeof(unsigned long long)));
+  }
+  if (g_dbg_buf[dev] != nullptr)
+    LP_CUDA_TRY(cudaMemset(g_dbg_buf[dev], 0, (size_t)kDbgKinds * 256 * 8 * sizeof(unsigned long long)));
+  g_dbg_on.store(on != 0);
+  return LP_OK;
+}
+
+int lp_debug_read(unsigned long long* out) {
+  int dev = 0;
+  LP_CUDA_TRY(cudaGetDevice(&dev));
+  if (out == nullptr) return fail(LP_EINVAL, "null out");
+  if (dev < 0 || dev >= kMaxDevices || g_dbg_buf[dev] == nullptr) return fail(LP_EINVAL, "debug counters not enabled");
+  std::vector<unsigned long long> h((size_t)kDbgKinds * 256 * 8);
+  LP_CUDA_TRY(cudaMemcpy(h.data(), g_dbg_buf[dev], h.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+  for (int k = 0; k < kDbgKinds; ++k)
+    for (int i = 0; i < 8; ++i) {
+      unsigned long long t = 0;
+      for (int c = 0; c < 256; ++c) t += h[((size_t)k * 256 + c) * 8 + i];
+      out[k * 8 + i] = t;
+    }
+  return LP_OK;
+}
 
 int lp_device_pairs(void) {
   DeviceInfo* di = nullptr;

@@ -92,7 +92,15 @@ struct EpiParams {
 struct GemmParams {
   GemmSched s;
   EpiParams e;
+  // Optional pipeline counters (nullptr = off), 8 per CTA, accumulated with atomicAdd:
+  // [0] producer cycles waiting for a free stage, [1] MMA cycles waiting for loaded stages,
+  // [2] MMA cycles waiting for a free accumulator, [3] epilogue-warp cycles waiting for a
+  // full accumulator (warp 2), [4] MMA-thread cycles from start to drain, [5] K blocks
+  // issued, [6] epilogue-warp cycles from accumulator ready to hand-back (warp 2), [7] tiles.
+  unsigned long long* dbg;
 };
+
+__device__ __forceinline__ unsigned long long clk64() { return (unsigned long long)clock64(); }
 
 struct Unit {
   int m_tile, group, split;
@@ -228,6 +236,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (h) tma_load_2d_pair_hint(dst, m, bar, x, y, pol); else tma_load_2d_pair(dst, m, bar, x, y);
       };
       uint32_t it = 0;
+      unsigned long long dbg_wait_prod = 0;
       int last_stage_phase[NS];
 #pragma unroll
       for (int s = 0; s < NS; ++s) last_stage_phase[s] = -1;
@@ -240,10 +249,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int kb = un.kb_begin; kb < un.kb_begin + un.kb_count; ++kb, ++it) {
             const int s = it % NS;
             const uint32_t ph = (it / NS) & 1;
+            const unsigned long long w0 = P.dbg ? clk64() : 0ull;
             if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, DEV_TIMEOUT_PRODUCER)) {
               ok = false;
               break;
             }
+            if (P.dbg) dbg_wait_prod += clk64() - w0;
             last_stage_phase[s] = (int)ph;
             uint8_t* a = stages + s * C::STAGE_BYTES;
             uint8_t* b = a + A_STAGE_BYTES;
@@ -283,6 +294,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
+      if (P.dbg) atomicAdd(&P.dbg[blockIdx.x * 8 + 0], dbg_wait_prod);
       // Never leave with TMA writes in flight into this CTA's shared memory. The leader's
       // full barriers count both CTAs' bytes; in a healthy run every load was consumed by
       // an MMA (so these waits return at once), and after a timeout the wait limit is
@@ -307,23 +319,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc = make_idesc_bf16(C::BM, BN, A_MN, B_MN);
       uint32_t it = 0, tc = 0;
       bool ok = true;
+      const unsigned long long t_start = P.dbg ? clk64() : 0ull;
+      unsigned long long dbg_full = 0, dbg_tempty = 0, dbg_kb = 0, dbg_tiles = 0;
       for (int u = unit0; ok && u < S.num_units; u += unit_step) {
         const Unit un = get_unit(S, u);
         for (int nt = un.n_begin; ok && nt < un.n_begin + un.n_count; ++nt, ++tc) {
           const int buf = tc & 1;
           const uint32_t tph = (tc >> 1) & 1;
+          const unsigned long long w0 = P.dbg ? clk64() : 0ull;
           if (!mbar_wait_bounded(&tempty_bar[buf], tph ^ 1, abort_flag, DEV_TIMEOUT_MMA)) {
             ok = false;
             break;
+          }
+          if (P.dbg) {
+            dbg_tempty += clk64() - w0;
+            dbg_tiles += 1;
           }
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
           for (int kb = 0; kb < un.kb_count; ++kb, ++it) {
             const int s = it % NS;
             const uint32_t ph = (it / NS) & 1;
+            const unsigned long long w1 = P.dbg ? clk64() : 0ull;
             if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, DEV_TIMEOUT_MMA)) {
               ok = false;
               break;
+            }
+            if (P.dbg) {
+              dbg_full += clk64() - w1;
+              dbg_kb += 1;
             }
             tc_fence_after();
             const uint32_t a_addr = smem_u32(stages + s * C::STAGE_BYTES);
@@ -359,6 +383,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
+      if (P.dbg) {
+        unsigned long long* d = &P.dbg[blockIdx.x * 8];
+        atomicAdd(d + 1, dbg_full);
+        atomicAdd(d + 2, dbg_tempty);
+        atomicAdd(d + 4, clk64() - t_start);
+        atomicAdd(d + 5, dbg_kb);
+        atomicAdd(d + 7, dbg_tiles);
+      }
       // Drain: every MMA issued by this thread completes before TMEM is released.
       if constexpr (CG == 1) mma_commit(done_bar); else mma_commit_pair(mapa_shared(smem_u32(done_bar), 0));
       const uint64_t t0 = globaltimer_ns();
@@ -386,6 +418,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float k1 = HAS_CAP ? 2.0f * kLog2e / cap : 0.f;  // x -> 2x/c in base 2
     const float c2 = HAS_CAP ? cap * kLog2e : 0.f;        // c in base 2
     bool ok = true;
+    const bool dbg_warp = P.dbg != nullptr && warp == 2 && lane == 0;
+    unsigned long long dbg_wait = 0, dbg_busy = 0, dbg_t = 0;
 
     for (int u = unit0; ok && u < S.num_units; u += unit_step) {
       const Unit un = get_unit(S, u);
@@ -410,14 +444,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           l2 = E.stats[row] * kLog2e + log2f(E.stats[E.stats_ld + row]);
         }
       }
+      const float ng = -gv, ng4 = -4.f * gv;  // dZ of a non-target column, without / with softcap
+      const float c2ml2 = c2 - l2;
 
       for (int nt = un.n_begin; nt < un.n_begin + un.n_count; ++nt, ++tc) {
         const int buf = tc & 1;
         const uint32_t tph = (tc >> 1) & 1;
+        if (dbg_warp) dbg_t = clk64();
         // warp-uniform decision: tcgen05.ld below is .sync.aligned
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&tfull_bar[buf], tph, abort_flag, DEV_TIMEOUT_EPILOGUE))) {
           ok = false;
           break;
+        }
+        if (dbg_warp) {
+          const unsigned long long now = clk64();
+          dbg_wait += now - dbg_t;
+          dbg_t = now;
         }
         tc_fence_after();
         const uint32_t taddr = tmem_base + lane_base + (uint32_t)(buf * BN + h * (BN / 2));
@@ -434,13 +476,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int nvalid = S.N - col0;  // columns >= nvalid are vocabulary padding (warp-uniform)
             if (nvalid <= 0) continue;
             float mx0 = -INFINITY, mx1 = -INFINITY;
+            if (nvalid >= 32) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float x = __uint_as_float(r[j]);
-              float z = HAS_CAP ? fmaf(-2.f * c2, fast_rcp(1.f + fast_ex2(x * k1)), c2) : x * kLog2e;
-              z = (j < nvalid) ? z : -INFINITY;
-              r[j] = __float_as_uint(z);
-              if (j & 1) mx1 = fmaxf(mx1, z); else mx0 = fmaxf(mx0, z);
+              for (int j = 0; j < 32; ++j) {
+                const float x = __uint_as_float(r[j]);
+                const float z = HAS_CAP ? fmaf(-2.f * c2, fast_rcp(1.f + fast_ex2(x * k1)), c2) : x * kLog2e;
+                r[j] = __float_as_uint(z);
+                if (j & 1) mx1 = fmaxf(mx1, z); else mx0 = fmaxf(mx0, z);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float x = __uint_as_float(r[j]);
+                float z = HAS_CAP ? fmaf(-2.f * c2, fast_rcp(1.f + fast_ex2(x * k1)), c2) : x * kLog2e;
+                z = (j < nvalid) ? z : -INFINITY;
+                r[j] = __float_as_uint(z);
+                if (j & 1) mx1 = fmaxf(mx1, z); else mx0 = fmaxf(mx0, z);
+              }
             }
             const int tj = yl - col0;
             if ((unsigned)tj < 32u) {
@@ -471,30 +523,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_wait_ld(r);
             const int col0 = colh + pc * 32;
             const int tj = yl - col0;
-            // dZ = g * (onehot - 2^(z2 - l2)) * (1 - tanh^2); packed to bf16 pairs
+            // dZ = g * (onehot - p) * (1 - tanh^2) with p = 2^(z2 - l2). Per column, without the
+            // one-hot term: with r = 1 / (1 + e^(2x/c)), z2 = c2 - 2 c2 r, 1 - tanh^2 = 4 r (1 - r),
+            //   dZ = (-4 g) * r * (1 - r) * 2^(fma(-2 c2, r, c2 - l2)).
+            // The target column (at most one per row) adds g * (1 - tanh^2) afterwards.
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float x = __uint_as_float(r[j]);
+              if (HAS_CAP) {
+                const float rr = fast_rcp(1.f + fast_ex2(x * k1));
+                const float p = fast_ex2(fmaf(-2.f * c2, rr, c2ml2));
+                v[j] = ng4 * rr * (1.f - rr) * p;
+              } else {
+                v[j] = ng * fast_ex2(fmaf(x, kLog2e, -l2));
+              }
+            }
+            if ((unsigned)tj < 32u) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (j == tj) {
+                  const float x = __uint_as_float(r[j]);
+                  float chain = 1.f;
+                  if (HAS_CAP) {
+                    const float rr = fast_rcp(1.f + fast_ex2(x * k1));
+                    chain = 4.f * rr * (1.f - rr);
+                  }
+                  v[j] += gv * chain;
+                }
+              }
+            }
             uint32_t pk[16];
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              float v[2];
-#pragma unroll
-              for (int hh = 0; hh < 2; ++hh) {
-                const int jj = j + hh;
-                const float x = __uint_as_float(r[jj]);
-                float z, chain;
-                if (HAS_CAP) {
-                  const float rr = fast_rcp(1.f + fast_ex2(x * k1));
-                  z = fmaf(-2.f * c2, rr, c2);
-                  chain = 4.f * rr * (1.f - rr);
-                } else {
-                  z = x * kLog2e;
-                  chain = 1.f;
-                }
-                const float p = fast_ex2(z - l2);
-                const float onehot = (jj == tj) ? 1.f : 0.f;
-                v[hh] = gv * chain * (onehot - p);
-              }
-              pk[j >> 1] = pack_bf16x2(v[0], v[1]);
-            }
+            for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
             if (lane == 0) bulk_wait_read<1>();
             __syncwarp();
             uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
@@ -568,6 +629,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // hand the accumulator back to the MMA warp (in the leader for CG = 2)
         tc_fence_before();
         __syncwarp();
+        if (dbg_warp) dbg_busy += clk64() - dbg_t;
         if (lane == 0) {
           if constexpr (CG == 1)
             mbar_arrive(&tempty_bar[buf]);
@@ -585,6 +647,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (EPI != EPI_FWD_LSE) {
       if (lane == 0) bulk_wait<0>();  // all TMA stores of this warp complete before exit
       __syncwarp();
+    }
+    if (dbg_warp) {
+      atomicAdd(&P.dbg[blockIdx.x * 8 + 3], dbg_wait);
+      atomicAdd(&P.dbg[blockIdx.x * 8 + 6], dbg_busy);
     }
   }
 

@@ -74,6 +74,14 @@ LP_API long long lp_launch_count(void);
 LP_API int lp_set_cta_group(int cg);
 LP_API int lp_get_cta_group(void);
 
+/* Tuning aid: per-GEMM pipeline counters (cycles the TMA, MMA and epilogue warps wait on
+ * each barrier, summed over CTAs). lp_debug_enable(1) allocates and zeroes the counters of
+ * the current device; lp_debug_read fills out[5][8] (forward, dZ, dH, dW, other x
+ * {producer wait, MMA wait on loads, MMA wait on accumulator, epilogue wait, MMA-thread
+ * cycles, K blocks, epilogue busy, tiles}). */
+LP_API int lp_debug_enable(int on);
+LP_API int lp_debug_read(unsigned long long* out);
+
 /* CTA pairs of the pair GEMMs that can be resident on the current device (-1 on error). */
 LP_API int lp_device_pairs(void);
 
