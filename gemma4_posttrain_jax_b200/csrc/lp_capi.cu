@@ -372,6 +372,42 @@ BwdLayout bwd_layout(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int 
 }
 
 // --------------------------------------------------------------------------- launches
+}  // namespace
+
+// Work-unit counters of the GEMM kernels (each launch claims its units with atomicAdd on
+// one slot). Slots rotate so that launches in flight on different streams use different
+// counters; a launch zeroes its slot on its own stream just before it starts.
+constexpr int kSchedSlots = 4096;
+static __device__ unsigned int g_lp_sched[kSchedSlots];
+
+namespace {
+
+unsigned int* g_sched_ptr[kMaxDevices] = {};
+std::mutex g_sched_mu;
+std::atomic<unsigned> g_sched_next{0};
+
+int sched_slot(cudaStream_t st, unsigned int** out) {
+  int dev = 0;
+  LP_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(LP_EINVAL, "device ordinal %d out of range", dev);
+  unsigned int* base;
+  {
+    std::lock_guard<std::mutex> lk(g_sched_mu);
+    if (g_sched_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_lp_sched);
+      if (e != cudaSuccess || p == nullptr)
+        return fail(LP_ECUDA, "cudaGetSymbolAddress(work counters) on device %d: %s", dev, cudaGetErrorString(e));
+      g_sched_ptr[dev] = static_cast<unsigned int*>(p);
+    }
+    base = g_sched_ptr[dev];
+  }
+  unsigned int* slot = base + g_sched_next.fetch_add(1u) % kSchedSlots;
+  LP_CUDA_TRY(cudaMemsetAsync(slot, 0, sizeof(unsigned int), st));
+  *out = slot;
+  return LP_OK;
+}
+
 template <int CG, int EPI, bool A_MN, bool B_MN, bool CAP>
 int launch_gemm_cg(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
                    const GemmParams& p, const DeviceInfo* di, const char* tag) {
@@ -388,6 +424,7 @@ int launch_gemm_cg(cudaStream_t st, const CUtensorMap& a, const CUtensorMap& b, 
   const int grid = CG * std::max(1, std::min(p.s.num_units, workers(di, CG)));
   GemmParams pp = p;
   pp.dbg = dbg_ptr(tag);
+  if (int rc = sched_slot(st, &pp.sched)) return rc;
   ProfScope prof(st, tag);
   if constexpr (CG == 1) {
     kern<<<grid, NUM_THREADS, smem, st>>>(a, b, o, pp);

@@ -9,9 +9,10 @@
 //         traffic per MMA-FLOP drops by a third and the smem ring gets 6 stages instead of 4.
 //         Each CTA's TMEM holds the accumulator rows of its half of the M tile.
 //
-// Persistent CTAs (CG = 2: CTA pairs) walk a static round-robin list of work units. A unit
-// is one M tile (128*CG rows), a run of consecutive 256-column N tiles and a range of
-// 64-deep K blocks.
+// Persistent CTAs (CG = 2: CTA pairs) claim work units dynamically, in unit order, from an
+// atomic counter (so the units in flight form a compact window of the order, which keeps
+// the operands they share in L2). A unit is one M tile (128*CG rows), a run of consecutive
+// 256-column N tiles and a range of 64-deep K blocks.
 //
 //   warp 0      : TMA producer (one thread)  -> NUM_STAGES-deep smem ring
 //   warp 1      : TMEM allocator + MMA issuer (one thread; in the pair leader only)
@@ -98,6 +99,9 @@ struct GemmParams {
   // full accumulator (warp 2), [4] MMA-thread cycles from start to drain, [5] K blocks
   // issued, [6] epilogue-warp cycles from accumulator ready to hand-back (warp 2), [7] tiles.
   unsigned long long* dbg;
+  // Dynamic work distribution: units are claimed in order with atomicAdd on this counter
+  // (zero at launch), so the units in flight always form a compact window of the unit order.
+  unsigned int* sched;
 };
 
 __device__ __forceinline__ unsigned long long clk64() { return (unsigned long long)clock64(); }
@@ -155,8 +159,8 @@ __host__ __device__ constexpr int staging_bytes() {
 
 template <int CG, int EPI>
 __host__ __device__ constexpr int gemm_smem_bytes() {
-  // 1 KB alignment slack + stages + staging + barriers, TMEM slot and abort flag
-  return 1024 + Cfg<CG>::NUM_STAGES * Cfg<CG>::STAGE_BYTES + staging_bytes<EPI>() + 256;
+  // 1 KB alignment slack + stages + staging + barriers, work-unit ring, TMEM slot, abort flag
+  return 1024 + Cfg<CG>::NUM_STAGES * Cfg<CG>::STAGE_BYTES + staging_bytes<EPI>() + 512;
 }
 
 // Byte offset of 16-byte chunk c (0..3) of row r in a 64-byte-swizzled box of 64-byte rows
@@ -180,7 +184,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tfull_bar = bars + 2 * NS;   // [2]
   uint64_t* tempty_bar = tfull_bar + 2;  // [2]
   uint64_t* done_bar = tempty_bar + 2;   // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  // work-unit ring: the (pair leader's) producer claims units and publishes them here
+  constexpr int SR = 8;
+  uint64_t* sfull_bar = done_bar + 1;     // [SR] unit id written
+  uint64_t* sempty_bar = sfull_bar + SR;  // [SR] every consumer has read it (leader's copy counts)
+  volatile int* sched_u = reinterpret_cast<volatile int*>(sempty_bar + SR);  // [SR]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(sched_u) + SR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const GemmSched& S = P.s;
@@ -188,8 +197,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;  // position in the pair
   const bool leader = rank == 0;
-  const int unit0 = blockIdx.x / CG;                       // first unit of this CTA (pair)
-  const int unit_step = gridDim.x / CG;
+  // consumers of a ring entry: the MMA thread and the epilogue warps (+ the peer's
+  // producer and epilogue warps for a pair)
+  constexpr int kRingConsumers = CG == 1 ? 1 + EPI_WARPS : 2 * (1 + EPI_WARPS);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -201,6 +211,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&tempty_bar[b], EPI_WARPS * CG);
     }
     mbar_init(done_bar, 1);
+    for (int i = 0; i < SR; ++i) {
+      mbar_init(&sfull_bar[i], 1);
+      mbar_init(&sempty_bar[i], kRingConsumers);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -241,7 +255,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int s = 0; s < NS; ++s) last_stage_phase[s] = -1;
       bool ok = true;
-      for (int u = unit0; ok && u < S.num_units; u += unit_step) {
+      for (int i = 0; ok; ++i) {
+        const int slot = i % SR;
+        const uint32_t sph = (i / SR) & 1;
+        int u;
+        if (leader) {
+          // claim the next unit and publish it (to the peer CTA too)
+          const bool free_slot = CG == 1
+                                     ? mbar_wait_bounded(&sempty_bar[slot], sph ^ 1, abort_flag, DEV_TIMEOUT_PRODUCER)
+                                     : mbar_wait_bounded_cluster(&sempty_bar[slot], sph ^ 1, abort_flag,
+                                                                 DEV_TIMEOUT_PRODUCER);
+          if (!free_slot) break;
+          const unsigned claimed = atomicAdd(P.sched, 1u);
+          u = claimed < (unsigned)S.num_units ? (int)claimed : -1;
+          sched_u[slot] = u;
+          if constexpr (CG == 2) {
+            st_shared_cluster_u32(mapa_shared(smem_u32(const_cast<int*>(&sched_u[slot])), 1), (uint32_t)u);
+            mbar_arrive_remote(mapa_shared(smem_u32(&sfull_bar[slot]), 1));
+          }
+          mbar_arrive(&sfull_bar[slot]);
+        } else {
+          if (!mbar_wait_bounded_cluster(&sfull_bar[slot], sph, abort_flag, DEV_TIMEOUT_PRODUCER)) break;
+          u = sched_u[slot];
+          mbar_arrive_remote(mapa_shared(smem_u32(&sempty_bar[slot]), 0));
+        }
+        if (u < 0) break;
         const Unit un = get_unit(S, u);
         const int a_row = un.m_tile * C::BM + (int)rank * 128;
         for (int nt = un.n_begin; ok && nt < un.n_begin + un.n_count; ++nt) {
@@ -321,7 +359,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       const unsigned long long t_start = P.dbg ? clk64() : 0ull;
       unsigned long long dbg_full = 0, dbg_tempty = 0, dbg_kb = 0, dbg_tiles = 0;
-      for (int u = unit0; ok && u < S.num_units; u += unit_step) {
+      for (int i = 0; ok; ++i) {
+        const int slot = i % SR;
+        if (!mbar_wait_bounded(&sfull_bar[slot], (i / SR) & 1, abort_flag, DEV_TIMEOUT_MMA)) break;
+        const int u = sched_u[slot];
+        mbar_arrive(&sempty_bar[slot]);
+        if (u < 0) break;
         const Unit un = get_unit(S, u);
         for (int nt = un.n_begin; ok && nt < un.n_begin + un.n_count; ++nt, ++tc) {
           const int buf = tc & 1;
@@ -421,7 +464,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const bool dbg_warp = P.dbg != nullptr && warp == 2 && lane == 0;
     unsigned long long dbg_wait = 0, dbg_busy = 0, dbg_t = 0;
 
-    for (int u = unit0; ok && u < S.num_units; u += unit_step) {
+    for (int i = 0; ok; ++i) {
+      const int slot = i % SR;
+      const uint32_t sph = (i / SR) & 1;
+      const bool got = CG == 1 || leader
+                           ? mbar_wait_bounded(&sfull_bar[slot], sph, abort_flag, DEV_TIMEOUT_EPILOGUE)
+                           : mbar_wait_bounded_cluster(&sfull_bar[slot], sph, abort_flag, DEV_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, got)) break;
+      const int u = sched_u[slot];
+      __syncwarp();
+      if (lane == 0) {
+        if (CG == 1 || leader)
+          mbar_arrive(&sempty_bar[slot]);
+        else
+          mbar_arrive_remote(mapa_shared(smem_u32(&sempty_bar[slot]), 0));
+      }
+      if (u < 0) break;
       const Unit un = get_unit(S, u);
       const int row_base = un.m_tile * C::BM + (int)rank * 128 + q * 32;  // first row of this warp
       const int row = row_base + lane;
