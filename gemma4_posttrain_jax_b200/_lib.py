@@ -54,6 +54,12 @@ _SIG = {
         [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, ctypes.c_float, _P, _P, _P, _I64, _P, ctypes.c_int, _I64, _P,
          ctypes.c_size_t],
     ),
+    "lp_bwd_sum_counters": (ctypes.c_size_t, [_I64]),
+    "lp_bwd_sum": (
+        ctypes.c_int,
+        [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, ctypes.c_float, _P, _P, _P, _P, _I64, _P, _P, ctypes.c_int,
+         ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _I64, _P, ctypes.c_size_t],
+    ),
     "lp_compact_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
     "lp_compact": (
         ctypes.c_int,
@@ -63,6 +69,7 @@ _SIG = {
     "lp_scatter_rows": (
         ctypes.c_int, [_P, _P, _I64, _P, _I64, _I64, ctypes.c_int, _P, _I64, _I64, _I64, ctypes.c_int]
     ),
+    "lp_peer_barrier": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
 }
 EXPORTED_SYMBOLS = tuple(_SIG)
 

@@ -677,9 +677,22 @@ size_t lp_bwd_workspace_bytes(int64_t T, int64_t d, int64_t Vs, int64_t token_ch
          256;
 }
 
-int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
-           const int32_t* y, float softcap, const float* norm, const float* g, void* dH, int64_t ld_dh, void* dW,
-           int flags, int64_t token_chunk, void* workspace, size_t workspace_bytes) {
+}  // extern "C"
+
+namespace {
+
+// The dH sum over the vocabulary mesh inside the dH GEMM (lp_bwd_sum).
+struct MeshSum {
+  void* dh_mc;
+  unsigned* cnt_local;
+  unsigned* cnt_mc;
+  int rank, world;
+  unsigned long long limit_ns;
+};
+
+int bwd_impl(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
+             const int32_t* y, float softcap, const float* norm, const float* g, void* dH, int64_t ld_dh, void* dW,
+             int flags, int64_t token_chunk, void* workspace, size_t workspace_bytes, const MeshSum* ms) {
   int rc = check_common(H, T, d, ldh, W, Vs, y);
   if (rc) return rc;
   const bool want_dh = !(flags & LP_BWD_NO_DH), want_dw = !(flags & LP_BWD_NO_DW);
@@ -697,6 +710,11 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
     return LP_OK;
   }
   const int cg_dz = cta_group_for(CG_DZ), cg_dh = cta_group_for(CG_DH), cg_dw = cta_group_for(CG_DW);
+  if (ms != nullptr && want_dh) {
+    // chunks start on 256-row boundaries (the row-block counters are per 128 rows)
+    if (token_chunk <= 0) token_chunk = default_token_chunk(T, Vs);
+    if (token_chunk < T) token_chunk = std::max<int64_t>(256, token_chunk / 256 * 256);
+  }
   const BwdLayout L = bwd_layout(T, d, Vs, token_chunk, flags, workers(di, cg_dh), 128 * cg_dh);
   if (workspace == nullptr || workspace_bytes < L.total)
     return fail(LP_EWORKSPACE, "lp_bwd needs %zu workspace bytes, got %zu", L.total, workspace_bytes);
@@ -737,9 +755,26 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
       if ((rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, BK, 128, "dZ as A"))) return rc;
       if ((rc = map_bf16(&tb, W, d, Vs, d, 64, 64, "embedding as MN-major B"))) return rc;
       GemmParams p{};
-      p.s = plan_gemm(tcur, d, Vs, workers(di, cg_dh), true, 1, 128 * cg_dh);
+      const int wk = workers(di, cg_dh);
+      p.s = plan_gemm(tcur, d, Vs, wk, ms == nullptr, 1, 128 * cg_dh);
       char* dh_c = reinterpret_cast<char*>(dH) + (size_t)t0 * ld_dh * (dh_f32 ? 4 : 2);
-      if (p.s.k_splits == 1) {
+      if (ms != nullptr) {
+        // partial tiles stored (bf16) into this rank's copy, summed across ranks by the
+        // reduce items of the same launch
+        if ((rc = map_store_bf16(&to, dh_c, d, tcur, ld_dh, "dH partial store"))) return rc;
+        p.e.store_mode = STORE_BF16;
+        p.e.split_rows = 0;
+        p.s.red_lag = std::min(p.s.tiles_m, (int)cdiv(3 * (int64_t)wk, p.s.tiles_n) + 2);
+        p.s.num_units = p.s.tiles_m * p.s.tiles_n + p.s.tiles_m;
+        p.e.sum_mc = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(ms->dh_mc) + (size_t)t0 * ld_dh * 2);
+        p.e.sum_ld = ld_dh;
+        p.e.cnt_local = ms->cnt_local + t0 / 128;
+        p.e.cnt_mc = ms->cnt_mc + t0 / 128;
+        p.e.cnt_target = (unsigned)(ms->world * p.s.tiles_n * EPI_WARPS * cg_dh);
+        p.e.sum_rank = ms->rank;
+        p.e.sum_world = ms->world;
+        p.e.peer_limit_ns = ms->limit_ns;
+      } else if (p.s.k_splits == 1) {
         if (dh_f32) {
           if ((rc = map_store_f32(&to, dh_c, d, tcur, ld_dh, "dH store"))) return rc;
           p.e.store_mode = STORE_F32;
@@ -790,6 +825,37 @@ int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
     LP_LAUNCH_CHECK("f32_to_bf16_kernel");
   }
   return LP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
+           const int32_t* y, float softcap, const float* norm, const float* g, void* dH, int64_t ld_dh, void* dW,
+           int flags, int64_t token_chunk, void* workspace, size_t workspace_bytes) {
+  return bwd_impl(stream, H, T, d, ldh, W, Vs, v_off, y, softcap, norm, g, dH, ld_dh, dW, flags, token_chunk,
+                  workspace, workspace_bytes, nullptr);
+}
+
+size_t lp_bwd_sum_counters(int64_t T) { return T > 0 ? (size_t)cdiv(T, 128) + 2 : 0; }
+
+int lp_bwd_sum(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs,
+               int64_t v_off, const int32_t* y, float softcap, const float* norm, const float* g, void* dH,
+               void* dH_multicast, int64_t ld_dh, unsigned* counters, unsigned* counters_multicast, int rank,
+               int world, int timeout_ms, void* dW, int flags, int64_t token_chunk, void* workspace,
+               size_t workspace_bytes) {
+  if (flags & (LP_BWD_DH_F32 | LP_BWD_NO_DH))
+    return fail(LP_EINVAL, "lp_bwd_sum sums a bf16 dH: LP_BWD_DH_F32 / LP_BWD_NO_DH do not apply");
+  if (dH_multicast == nullptr || counters == nullptr || counters_multicast == nullptr)
+    return fail(LP_EINVAL, "null multicast dH or counters");
+  if (((reinterpret_cast<uintptr_t>(dH) | reinterpret_cast<uintptr_t>(dH_multicast)) & 15) != 0)
+    return fail(LP_EINVAL, "dH and its multicast address must be 16-byte aligned");
+  if (world < 1 || rank < 0 || rank >= world) return fail(LP_EINVAL, "bad rank %d / world %d", rank, world);
+  if (timeout_ms <= 0) return fail(LP_EINVAL, "timeout_ms must be positive");
+  const MeshSum ms{dH_multicast, counters, counters_multicast, rank, world, (unsigned long long)timeout_ms * 1000000ull};
+  return bwd_impl(stream, H, T, d, ldh, W, Vs, v_off, y, softcap, norm, g, dH, ld_dh, dW, flags, token_chunk,
+                  workspace, workspace_bytes, &ms);
 }
 
 int lp_gemm_bf16(void* stream, const void* A, int64_t M, int64_t K, int64_t lda, int a_mn, const void* B, int64_t N,
@@ -915,6 +981,20 @@ int lp_scatter_rows(void* stream, const void* src, int64_t src_stride, const int
                                                    rows_per_group, group_stride);
     LP_LAUNCH_CHECK("scatter_rows_elem_kernel");
   }
+  return LP_OK;
+}
+
+int lp_peer_barrier(void* stream, const unsigned long long* signal_pads, int rank, int world, int channel,
+                    int timeout_ms) {
+  if (signal_pads == nullptr) return fail(LP_EINVAL, "null signal_pads");
+  if (world < 1 || world > 1024 || rank < 0 || rank >= world) return fail(LP_EINVAL, "bad rank %d / world %d", rank, world);
+  if (channel < 0 || timeout_ms <= 0) return fail(LP_EINVAL, "bad channel %d or timeout %d ms", channel, timeout_ms);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int threads = (world + 31) / 32 * 32;
+  ProfScope prof(st, "peer_barrier");
+  peer_barrier_kernel<<<1, threads, 0, st>>>(signal_pads, rank, world, channel,
+                                             (unsigned long long)timeout_ms * 1000000ull);
+  LP_LAUNCH_CHECK("peer_barrier_kernel");
   return LP_OK;
 }
 

@@ -74,6 +74,11 @@ struct GemmSched {
   int bm;      // rows per M tile (128 * CG)
   int m_chunk; // > 0 (with n_fast = 0): units walk M in chunks of m_chunk tiles, all N groups
                // of a chunk before the next chunk, so the A rows CTAs re-read stay in L2
+  // > 0: cross-rank sum of the output (n_fast, one tile per unit, no K split). The work list
+  // holds one reduce item per M tile after the tiles: the reduce item of row block b follows
+  // the tiles of row block b + red_lag, so the block is normally complete on every rank by
+  // the time a CTA takes it.
+  int red_lag;
 };
 
 struct EpiParams {
@@ -86,6 +91,17 @@ struct EpiParams {
   const float* stats;    // DZ : [2][stats_ld] global (max, sum) in natural units
   long long stats_ld;    // DZ : row stride of stats
   int store_mode;        // STORE: STORE_BF16 / STORE_F32 / STORE_F32_ADD
+  // Cross-rank sum (sched red_lag > 0, STORE_BF16 into symmetric memory): every rank stores
+  // its partial tiles locally and counts them on the row block's counter in all ranks' copies
+  // (multimem.red); rank r then reduces its share of each block's rows (ld_reduce over all
+  // copies through the NVSwitch, f32 accumulation) and stores the sum to all copies.
+  __nv_bfloat16* sum_mc;        // multicast address of the output (row 0 of this launch)
+  long long sum_ld;             // output row stride (elements, multiple of 8)
+  unsigned* cnt_local;          // this rank's copy of the per-128-row-block tile counters
+  unsigned* cnt_mc;             // their multicast address
+  unsigned cnt_target;          // counter value of a complete block: world * tiles_n * EPI_WARPS * CG
+  int sum_rank, sum_world;
+  unsigned long long peer_limit_ns;  // bound of a wait for the other ranks' tiles
   int split_rows;        // STORE: output-row offset between K splits (partials)
   int a_l2, b_l2;        // L2 eviction priority of the A / B loads (L2_NORMAL / _EVICT_FIRST / _EVICT_LAST)
 };
@@ -110,10 +126,45 @@ struct Unit {
   int m_tile, group, split;
   int n_begin, n_count;
   int kb_begin, kb_count;
+  int red_block;  // >= 0: a reduce item of this row block (no tiles)
 };
 
 __device__ __forceinline__ Unit get_unit(const GemmSched& s, int u) {
   int m, g, ks;
+  if (s.red_lag > 0) {
+    // tiles and reduce items interleaved (see red_lag); tiles in n_fast order
+    const int tn = s.tiles_n, lag = s.red_lag;
+    int tile = -1, rb = -1;
+    if (u < lag * tn) {
+      tile = u;
+    } else {
+      const int j = u - lag * tn;
+      const int q = j / (tn + 1), r = j % (tn + 1);
+      if (q < s.tiles_m - lag) {
+        if (r < tn) tile = (q + lag) * tn + r; else rb = q;
+      } else {
+        rb = (s.tiles_m - lag) + (j - (s.tiles_m - lag) * (tn + 1));
+      }
+    }
+    Unit x;
+    x.split = 0;
+    x.kb_begin = 0;
+    x.kb_count = s.k_blocks;
+    if (tile >= 0) {
+      x.m_tile = tile / tn;
+      x.group = tile % tn;
+      x.n_begin = x.group;
+      x.n_count = 1;
+      x.red_block = -1;
+    } else {
+      x.m_tile = rb;
+      x.group = 0;
+      x.n_begin = 0;
+      x.n_count = 0;
+      x.red_block = rb;
+    }
+    return x;
+  }
   if (!s.n_fast && s.m_chunk > 0) {
     // chunk-major: (chunk, N group, M tile within the chunk); the last chunk may be short
     const int mc = s.m_chunk;
@@ -149,6 +200,7 @@ __device__ __forceinline__ Unit get_unit(const GemmSched& s, int u) {
   x.n_count = min(s.n_group, s.tiles_n - x.n_begin);
   x.kb_begin = ks * s.kb_per_split;
   x.kb_count = min(s.kb_per_split, s.k_blocks - x.kb_begin);
+  x.red_block = -1;
   return x;
 }
 
@@ -694,8 +746,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           else
             mbar_arrive_remote(mapa_shared(smem_u32(&tempty_bar[buf]), 0));
         }
+        if (EPI == EPI_STORE && E.cnt_mc != nullptr) {
+          // this warp's rows of the partial tile are in this rank's memory: count them on the
+          // row block's counter in every rank's copy
+          if (lane == 0) {
+            bulk_wait<0>();
+            fence_proxy_async_global();
+            multimem_red_add_release_u32(E.cnt_mc + (size_t)un.m_tile * (C::BM / 128), 1u);
+          }
+          __syncwarp();
+        }
       }
       if (!ok) break;
+
+      if (EPI == EPI_STORE && un.red_block >= 0) {
+        // Reduce item: once every rank has stored all tiles of the row block, sum this rank's
+        // share of its rows over all ranks' copies (ld_reduce through the NVSwitch) and store
+        // the sum to every copy. The pair's CTAs split the share.
+        const int b = un.red_block;
+        bool ready = true;
+        if (lane == 0)
+          ready = wait_counter_bounded(E.cnt_local + (size_t)b * (C::BM / 128), E.cnt_target, abort_flag,
+                                       E.peer_limit_ns);
+        if (!__shfl_sync(0xffffffffu, (int)ready, 0)) {
+          ok = false;
+          break;
+        }
+        const int lo = b * C::BM + (E.sum_rank * C::BM) / E.sum_world;
+        const int hi = b * C::BM + ((E.sum_rank + 1) * C::BM) / E.sum_world;
+        const int r0 = lo + ((hi - lo) * (int)rank) / CG;
+        const int r1 = min(lo + ((hi - lo) * ((int)rank + 1)) / CG, S.M);
+        const int vpr = S.N >> 3;  // 16-byte vectors per row
+        const int nv = r0 < r1 ? (r1 - r0) * vpr : 0;
+        constexpr int NT = EPI_WARPS * 32;
+        for (int v0 = ew * 32 + lane; v0 < nv; v0 += 4 * NT) {
+          uint4 acc[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int v = v0 + k * NT;
+            if (v < nv) acc[k] = multimem_ld_reduce_bf16x8(E.sum_mc + (size_t)(r0 + v / vpr) * E.sum_ld + (v % vpr) * 8);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int v = v0 + k * NT;
+            if (v < nv) multimem_st_bf16x8(E.sum_mc + (size_t)(r0 + v / vpr) * E.sum_ld + (v % vpr) * 8, acc[k]);
+          }
+        }
+      }
 
       if constexpr (EPI == EPI_FWD_LSE) {
         // one (max, sum) partial per unit and column half
@@ -704,6 +801,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     if (EPI != EPI_FWD_LSE) {
       if (lane == 0) bulk_wait<0>();  // all TMA stores of this warp complete before exit
+      // the multicast stores are performed at system scope before the kernel ends, so a
+      // peer barrier after this launch publishes them
+      if (E.cnt_mc != nullptr) fence_sys();
       __syncwarp();
     }
     if (dbg_warp) {

@@ -13,7 +13,14 @@
 namespace lpk {
 
 // Error codes recorded by kernels in g_lp_device_error (first error wins).
-enum : int { DEV_OK = 0, DEV_TIMEOUT_PRODUCER = 1, DEV_TIMEOUT_MMA = 2, DEV_TIMEOUT_EPILOGUE = 3, DEV_TIMEOUT_DRAIN = 4 };
+enum : int {
+  DEV_OK = 0,
+  DEV_TIMEOUT_PRODUCER = 1,
+  DEV_TIMEOUT_MMA = 2,
+  DEV_TIMEOUT_EPILOGUE = 3,
+  DEV_TIMEOUT_DRAIN = 4,
+  DEV_TIMEOUT_PEER = 5  // a peer rank never reached lp_peer_barrier / never finished its tiles
+};
 
 }  // namespace lpk
 
@@ -295,6 +302,64 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 
 // ----------------------------------------------------------------------------- CTA pairs (cta_group::2)
 namespace lpk {
+
+__device__ __forceinline__ void ld_shared_v4f(uint32_t addr, float& a, float& b, float& c, float& d) {
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(a), "=f"(b), "=f"(c), "=f"(d) : "r"(addr) : "memory");
+}
+
+// NVLS multicast memory operations. `mc` is a multicast address: the NVSwitch applies the
+// operation to every GPU's copy of the buffer (st, red) or reads all copies and returns
+// their sum (ld_reduce; bf16 pairs accumulated in f32 inside the switch).
+__device__ __forceinline__ uint4 multimem_ld_reduce_bf16x8(const void* mc) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+
+__device__ __forceinline__ void multimem_st_bf16x8(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Adds v to a u32 in every copy; release: this thread's earlier writes are visible first.
+__device__ __forceinline__ void multimem_red_add_release_u32(unsigned* mc, unsigned v) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Wait (bounded by limit_ns) until *p >= target; on expiry raise the CTA's abort flag and
+// record DEV_TIMEOUT_PEER.
+__device__ __forceinline__ bool wait_counter_bounded(const unsigned* p, unsigned target, volatile int* abort,
+                                                     unsigned long long limit_ns) {
+  if (ld_acquire_sys_u32(p) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+      if (ld_acquire_sys_u32(p) >= target) return true;
+      __nanosleep(100);
+    }
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      *abort = 1;
+      record_device_error(DEV_TIMEOUT_PEER);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

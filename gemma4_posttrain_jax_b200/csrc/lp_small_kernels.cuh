@@ -246,6 +246,40 @@ __global__ void scatter_rows_f32_to_bf16_kernel(const float* __restrict__ src, l
   }
 }
 
+// Barrier of `world` ranks through their signal pads (peer-mapped, zero-initialised u32
+// slots; pads[p] is this process's address of rank p's pad). Rank r sets slot
+// [channel][r] of every pad from 0 to 1 (waiting until the previous signal there was
+// consumed), then waits for slot [channel][p] of its own pad to hold 1 and resets it, for
+// every p. Waits are bounded by limit_ns; on expiry the kernel records DEV_TIMEOUT_PEER and
+// returns. The system-scope fences order this rank's earlier writes (multicast reductions
+// included) before its signals, and the peers' writes before what follows the barrier.
+__global__ void peer_barrier_kernel(const unsigned long long* __restrict__ pads, int rank, int world, int channel,
+                                    unsigned long long limit_ns) {
+  const int p = threadIdx.x;
+  if (p < world) {
+    unsigned int* peer = reinterpret_cast<unsigned int*>(pads[p]) + (size_t)channel * world + rank;
+    unsigned int* own = reinterpret_cast<unsigned int*>(pads[rank]) + (size_t)channel * world + p;
+    fence_sys();
+    const uint64_t t0 = globaltimer_ns();
+    bool ok = true;
+    while (atomicCAS_system(peer, 0u, 1u) != 0u) {
+      if (globaltimer_ns() - t0 > limit_ns) {
+        record_device_error(DEV_TIMEOUT_PEER);
+        ok = false;
+        break;
+      }
+    }
+    while (ok && atomicCAS_system(own, 1u, 0u) != 1u) {
+      if (globaltimer_ns() - t0 > limit_ns) {
+        record_device_error(DEV_TIMEOUT_PEER);
+        break;
+      }
+    }
+    fence_sys();
+  }
+  __syncthreads();
+}
+
 // Element-wise fallback layout for rows that are not 16-byte multiples (e.g. logps).
 __global__ void scatter_rows_elem_kernel(const uint8_t* __restrict__ src, long long src_stride,
                                          const int32_t* __restrict__ pos, long long slots, long long width,

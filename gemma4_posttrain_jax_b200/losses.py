@@ -20,7 +20,7 @@ import torch
 
 from . import ops
 from .phase_timer import phase
-from .sharding import VocabMesh, all_gather_stats, all_reduce_sum, vocab_offset
+from .sharding import VocabMesh, all_gather_stats, all_reduce_sum, dh_sum_buffer, peer_timeout_ms, vocab_offset
 
 
 # A backward skips the rows whose upstream gradient is exactly zero (they add nothing to dH
@@ -51,27 +51,51 @@ def _gather_rows(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
     return ops.scatter_rows(src.contiguous(), idx, out)
 
 
-def _backward_rows(embed, H, y, softcap, norm, g, *, vocab_offset, need_dh, need_dw, dh_dtype, dw_dtype,
+def _backward_rows(embed, H, y, softcap, norm, g, *, mesh, vocab_offset, need_dh, need_dw, dh_dtype, dw_dtype,
                    token_chunk, skip_zero_grad):
-    """shard_backward on the rows with nonzero g; returns (dH rows in compact order or None,
-    dW, pos) where pos maps every row to its dH row (-1 = zero row), or pos None (dense)."""
+    """shard_backward on the rows with nonzero g, with the dH partials summed over the mesh.
+
+    Returns (dH rows in compact order or None, dW, pos, shared): pos maps every row to its dH
+    row (-1 = zero row), or is None (dense). With more than one shard the sum runs inside the
+    dH GEMM through the mesh's NVLS multicast buffer when available -- dH is then a view of
+    that buffer (``shared`` True: copy it out before the next backward) -- else as an
+    all-reduce after the GEMM.
+    """
     sel = _nonzero_grad_rows(g) if skip_zero_grad else None
     if sel is None:
-        dH, dW = ops.shard_backward(embed, H, y, softcap, norm, g, vocab_offset=vocab_offset, need_dh=need_dh,
-                                    need_dw=need_dw, dh_dtype=dh_dtype, dw_dtype=dw_dtype, token_chunk=token_chunk)
-        return dH, dW, None
-    idx, pos, m = sel
-    if m == 0:
-        dW = torch.zeros(embed.shape, dtype=dw_dtype, device=embed.device) if need_dw else None
-        dH = torch.zeros((0, H.shape[-1]), dtype=dh_dtype, device=H.device) if need_dh else None
-        return dH, dW, pos
-    Hz = _gather_rows(H.reshape(-1, H.shape[-1]), idx)
-    yz = _gather_rows(y.reshape(-1).to(torch.int32).view(torch.float32), idx).view(torch.int32)
-    gz = _gather_rows(g.reshape(-1).to(torch.float32), idx)
-    nz = torch.stack([_gather_rows(norm[0].contiguous(), idx), _gather_rows(norm[1].contiguous(), idx)])
+        idx = pos = None
+        rows = H.reshape(-1, H.shape[-1]).shape[0]
+    else:
+        idx, pos, rows = sel
+        if rows == 0:
+            dW = torch.zeros(embed.shape, dtype=dw_dtype, device=embed.device) if need_dw else None
+            dH = torch.zeros((0, H.shape[-1]), dtype=dh_dtype, device=H.device) if need_dh else None
+            return dH, dW, pos, False
+    if idx is not None:
+        Hz = _gather_rows(H.reshape(-1, H.shape[-1]), idx)
+        yz = _gather_rows(y.reshape(-1).to(torch.int32).view(torch.float32), idx).view(torch.int32)
+        gz = _gather_rows(g.reshape(-1).to(torch.float32), idx)
+        nz = torch.stack([_gather_rows(norm[0].contiguous(), idx), _gather_rows(norm[1].contiguous(), idx)])
+    else:
+        Hz, yz, gz, nz = H, y, g, norm
+    P = mesh.size if mesh is not None else 1
+    buf = dh_sum_buffer(mesh, rows, H.shape[-1], H.device) if (need_dh and P > 1) else None
+    if buf is not None:
+        timeout = peer_timeout_ms()
+        buf.counters[: int(ops.bwd_sum_counters(rows))].zero_()
+        ops.peer_barrier(buf, timeout)  # every rank's counters are zero and its previous dH read
+        dH, dW = ops.shard_backward(embed, Hz, yz, softcap, nz, gz, vocab_offset=vocab_offset, need_dh=True,
+                                    need_dw=need_dw, dh_dtype=torch.bfloat16, dw_dtype=dw_dtype,
+                                    token_chunk=token_chunk, dh_mesh_sum=buf)
+        with phase("dh_peer_barrier"):
+            ops.peer_barrier(buf, timeout)  # every rank's share of the sum has landed everywhere
+        return dH, dW, pos, True
     dH, dW = ops.shard_backward(embed, Hz, yz, softcap, nz, gz, vocab_offset=vocab_offset, need_dh=need_dh,
                                 need_dw=need_dw, dh_dtype=dh_dtype, dw_dtype=dw_dtype, token_chunk=token_chunk)
-    return dH, dW, pos
+    if dH is not None and P > 1:
+        with phase("dh_all_reduce"):
+            all_reduce_sum(dH, mesh)
+    return dH, dW, pos, False
 
 
 def _validate(embed: torch.Tensor, hidden: torch.Tensor, targets: torch.Tensor, vocab_chunk: int, sequence_chunk: int):
@@ -129,13 +153,14 @@ class _CudaTokenLogps(torch.autograd.Function):
         # Shards sum their dH partials in the hidden dtype, as the reference's psum of the
         # bf16 cotangent does (losses.py:253-259 transposed); dh_reduce_f32 sums in f32 instead.
         dh_dtype = torch.float32 if (P > 1 and ctx.dh_reduce_f32) else torch.bfloat16
-        dH, dW, pos = _backward_rows(
+        dH, dW, pos, shared = _backward_rows(
             embed,
             hidden2d,
             targets1d,
             ctx.softcap,
             norm,
             g,
+            mesh=mesh,
             vocab_offset=ctx.offset,
             need_dh=need_dh,
             need_dw=need_dw,
@@ -144,15 +169,12 @@ class _CudaTokenLogps(torch.autograd.Function):
             token_chunk=ctx.token_chunk,
             skip_zero_grad=ctx.skip_zero_grad,
         )
-        if dH is not None and P > 1:
-            with phase("dh_all_reduce"):
-                all_reduce_sum(dH, mesh)
         if dH is not None and pos is not None:
             # back to one row per token: rows with zero upstream gradient get zero
             full = torch.empty(hidden2d.shape, dtype=hidden2d.dtype, device=hidden2d.device)
             dH = ops.scatter_rows(dH, pos, full)
-        elif dH is not None and dH.dtype != hidden2d.dtype:
-            dH = dH.to(hidden2d.dtype)
+        elif dH is not None and (dH.dtype != hidden2d.dtype or shared):
+            dH = dH.to(hidden2d.dtype, copy=True)
         return dW, dH, None, None, None, None, None, None, None
 
 
@@ -247,8 +269,8 @@ class _CompletionLogps(torch.autograd.Function):
         if n > 0 and (need_dw or need_dh):
             gc = torch.empty((n,), dtype=torch.float32, device=g.device)
             ops.scatter_rows(g.reshape(-1).to(torch.float32).contiguous(), idx_n, gc)  # gc[i] = g[idx[i]]
-            dHc, dW, posz = _backward_rows(
-                embed, Hn, yn, softcap, norm, gc, vocab_offset=off, need_dh=need_dh, need_dw=need_dw,
+            dHc, dW, posz, _ = _backward_rows(
+                embed, Hn, yn, softcap, norm, gc, mesh=mesh, vocab_offset=off, need_dh=need_dh, need_dw=need_dw,
                 dh_dtype=torch.float32 if (P > 1 and dh_reduce_f32) else torch.bfloat16, dw_dtype=embed.dtype,
                 token_chunk=token_chunk, skip_zero_grad=skip_zero_grad,
             )
@@ -256,9 +278,6 @@ class _CompletionLogps(torch.autograd.Function):
                 # slot -> compact row -> nonzero-gradient row (or -1)
                 pos = torch.where(pos >= 0, posz[pos.clamp(min=0).long()], torch.full_like(pos, -1))
             if dHc is not None:
-                if P > 1:
-                    with phase("dh_all_reduce"):
-                        all_reduce_sum(dHc, mesh)
                 with phase("dh_zero_fill"):
                     # rows outside the response slice get 0; the scatter writes every slice row
                     dhidden = torch.empty(hshape, dtype=hdtype, device=g.device)

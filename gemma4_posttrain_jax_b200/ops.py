@@ -127,8 +127,15 @@ def shard_backward(
     dw_dtype: torch.dtype = torch.float32,
     token_chunk: int | None = None,
     dh_out: torch.Tensor | None = None,
+    dh_mesh_sum=None,
 ) -> tuple[torch.Tensor | None, torch.Tensor | None]:
-    """``lp_bwd`` on one vocabulary shard: (dH [T, d] partial over this shard, dW [Vs, d])."""
+    """``lp_bwd`` on one vocabulary shard: (dH [T, d] partial over this shard, dW [Vs, d]).
+
+    With ``dh_mesh_sum`` (a ``sharding.DhSumBuffer`` with at least T rows; every rank makes
+    the same call between two ``peer_barrier`` calls, its counters zeroed before the first)
+    this is ``lp_bwd_sum``: the returned dH is this rank's bf16 copy, which holds the sum over
+    the mesh's shards once the second barrier has passed.
+    """
     dev = _require_cuda(embed, hidden, targets, norm, grad_logp)
     _check_bf16("embedding", embed)
     _check_bf16("hidden", hidden)
@@ -144,7 +151,11 @@ def shard_backward(
     nrm = norm.reshape(2, -1).to(torch.float32).contiguous()
     flags = 0
     dH = dW = None
-    if need_dh:
+    if need_dh and dh_mesh_sum is not None:
+        if dh_mesh_sum.rows < T or dh_mesh_sum.d != d or dh_dtype != torch.bfloat16:
+            raise ValueError("dh_mesh_sum needs a buffer of at least [T, d] rows and a bf16 dH")
+        dH = dh_mesh_sum.local(T)
+    elif need_dh:
         if dh_out is not None:
             if dh_out.shape != (T, d) or dh_out.dtype != dh_dtype or dh_out.stride(-1) != 1:
                 raise ValueError("dh_out must be a [T, d] row-major tensor of dh_dtype")
@@ -165,6 +176,17 @@ def shard_backward(
     ws, wsp, wsn = _workspace(lib.lp_bwd_workspace_bytes(T, d, Vs, chunk, flags), dev)
     cap = float(softcap) if softcap is not None else 0.0
     ld_dh = int(dH.stride(0)) if dH is not None and T > 1 else d
+    if need_dh and dh_mesh_sum is not None:
+        from .sharding import peer_timeout_ms  # noqa: PLC0415
+
+        m = dh_mesh_sum
+        rc = lib.lp_bwd_sum(
+            _stream(dev), _ptr(h2), T, d, ldh, _ptr(w), Vs, int(vocab_offset), _ptr(y), cap, _ptr(nrm), _ptr(g),
+            _ptr(dH), ctypes.c_void_p(m.dh_mc), ld_dh, _ptr(m.counters), ctypes.c_void_p(m.counters_mc), m.rank,
+            m.world, peer_timeout_ms(), _ptr(dW), flags, chunk, wsp, wsn,
+        )
+        _lib.check(rc, "lp_bwd_sum")
+        return dH, dW
     rc = lib.lp_bwd(
         _stream(dev), _ptr(h2), T, d, ldh, _ptr(w), Vs, int(vocab_offset), _ptr(y), cap, _ptr(nrm), _ptr(g), _ptr(dH),
         ld_dh, _ptr(dW), flags, chunk, wsp, wsn,
@@ -262,3 +284,17 @@ def scatter_rows(src: torch.Tensor, pos: torch.Tensor, out: torch.Tensor) -> tor
     )
     _lib.check(rc, "lp_scatter_rows")
     return out
+
+
+def peer_barrier(buf, timeout_ms: int) -> None:
+    """``lp_peer_barrier`` over the signal pads of a ``sharding.DhSumBuffer``, on the current
+    stream of its device (every rank of the mesh must make the same calls in the same order)."""
+    lib = _lib.load()
+    rc = lib.lp_peer_barrier(_stream(buf.device), ctypes.c_void_p(buf.pads_dev), buf.rank, buf.world, buf.channel,
+                             int(timeout_ms))
+    _lib.check(rc, "lp_peer_barrier")
+
+
+def bwd_sum_counters(rows: int) -> int:
+    """Number of u32 row-block counters ``lp_bwd_sum`` uses for ``rows`` rows."""
+    return int(_lib.load().lp_bwd_sum_counters(int(rows)))

@@ -10,14 +10,17 @@ NCCL collectives (gloo on CPU for the host-logic tests):
 
   * all-gather of the per-shard (max, sum, owned target logit) triples, 12 bytes/token,
     merged on the device by ``lp_combine``;
-  * sum of the per-shard dH partials (all-reduce, or reduce-scatter when the caller's
-    hidden states are batch-sharded);
+  * sum of the per-shard dH partials: inside the dH GEMM through an NVLS multicast buffer
+    (``DhSumBuffer``, multimem reductions from the GEMM epilogue) where the GPUs support
+    it, else an NCCL all-reduce (reduce-scatter when the caller's hidden states are
+    batch-sharded);
   * optional all-gather of batch-sharded hidden rows / targets before the head.
 dW never leaves its shard.
 """
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -124,3 +127,88 @@ def reduce_scatter_rows(full: torch.Tensor, mesh: VocabMesh) -> torch.Tensor:
         return out
     dist.all_reduce(x, op=dist.ReduceOp.SUM, group=mesh.group)
     return x[mesh.rank * n : (mesh.rank + 1) * n].clone()
+
+
+# ----------------------------------------------------------------------------- multicast dH sum
+# Signal-pad row used by lp_peer_barrier (row 0 is left to torch's own symmetric-memory ops).
+_BARRIER_CHANNEL = 1
+_DH_BUFFERS: dict[tuple, "DhSumBuffer"] = {}
+_MULTICAST_UNAVAILABLE: set[tuple] = set()
+
+
+def dh_reduce_mode(mesh: VocabMesh | None) -> str:
+    """How the dH partials are summed across shards: "none" (one shard), "multimem" (inside
+    the dH GEMM through an NVLS multicast buffer) or "nccl" (all-reduce after it).
+    ``LP_B200_DH_REDUCE=nccl`` forces the all-reduce."""
+    if mesh is None or mesh.size == 1:
+        return "none"
+    if os.environ.get("LP_B200_DH_REDUCE", "multimem") != "multimem" or not _is_nccl(mesh):
+        return "nccl"
+    return "multimem"
+
+
+def peer_timeout_ms() -> int:
+    """Bound of every device-side wait of lp_peer_barrier (``LP_B200_PEER_TIMEOUT_MS``)."""
+    return max(1, int(os.environ.get("LP_B200_PEER_TIMEOUT_MS", "60000")))
+
+
+class DhSumBuffer:
+    """Symmetric memory bound to an NVLS multicast object on every rank of the mesh: a bf16
+    [rows, d] dH buffer and the u32 row-block counters of ``lp_bwd_sum``. The dH GEMM stores
+    each rank's partial tiles into its own copy and sums them across the copies through the
+    NVSwitch, so every rank ends with the sum over vocabulary shards -- the psum of the dH
+    partials (``losses.py:253-259`` transposed) done while the GEMM runs."""
+
+    def __init__(self, mesh: VocabMesh, rows: int, d: int, device: torch.device):
+        import torch.distributed._symmetric_memory as symm_mem  # noqa: PLC0415 - CUDA + NCCL only
+
+        from . import _lib  # noqa: PLC0415
+
+        group = mesh.group if mesh.group is not None else dist.group.WORLD
+        self.rows, self.d, self.device = int(rows), int(d), device
+        self.n_counters = int(_lib.load().lp_bwd_sum_counters(self.rows))
+        dh_bytes = -(-self.rows * self.d * 2 // 4096) * 4096
+        total = dh_bytes + -(-self.n_counters * 4 // 4096) * 4096
+        self.storage = symm_mem.empty((total,), dtype=torch.uint8, device=device)
+        self.dh = self.storage[: self.rows * self.d * 2].view(torch.bfloat16).view(self.rows, self.d)
+        self.counters = self.storage[dh_bytes : dh_bytes + self.n_counters * 4].view(torch.int32)
+        self.counters.zero_()
+        self.handle = symm_mem.rendezvous(self.storage, group)
+        mc = int(self.handle.multicast_ptr)
+        if mc == 0:
+            raise RuntimeError("symmetric memory has no multicast mapping on this system")
+        if (_BARRIER_CHANNEL + 1) * self.handle.world_size * 4 > self.handle.signal_pad_size:
+            raise RuntimeError("signal pad too small for the barrier channel")
+        self.dh_mc = mc
+        self.counters_mc = mc + dh_bytes
+        self.pads_dev = int(self.handle.signal_pad_ptrs_dev)
+        self.rank, self.world = int(self.handle.rank), int(self.handle.world_size)
+        self.channel = _BARRIER_CHANNEL
+
+    def local(self, rows: int) -> torch.Tensor:
+        """This rank's copy of the first ``rows`` dH rows (the sum, after the second barrier)."""
+        return self.dh[:rows]
+
+
+def dh_sum_buffer(mesh: VocabMesh, rows: int, d: int, device: torch.device) -> DhSumBuffer | None:
+    """The mesh's multicast dH buffer with room for ``rows`` x ``d`` (collective when it has to
+    grow: every rank holds the same row count because the upstream gradient is replicated),
+    or None where the multicast path is off or the system has no NVLS multicast."""
+    if dh_reduce_mode(mesh) != "multimem":
+        return None
+    gkey = (id(mesh.group), device.index)
+    if gkey in _MULTICAST_UNAVAILABLE:
+        return None
+    key = (*gkey, int(d))
+    buf = _DH_BUFFERS.get(key)
+    if buf is None or buf.rows < rows:
+        grow = max(int(rows), -(-int(rows * 5 // 4) // 1024) * 1024)
+        _DH_BUFFERS.pop(key, None)
+        buf = None
+        try:
+            buf = DhSumBuffer(mesh, grow, d, device)
+        except (RuntimeError, ImportError):
+            _MULTICAST_UNAVAILABLE.add(gkey)
+            return None
+        _DH_BUFFERS[key] = buf
+    return buf

@@ -165,6 +165,31 @@ LP_API int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh
            const int32_t* y, float softcap, const float* norm, const float* g, void* dH, int64_t ld_dh, void* dW,
            int flags, int64_t token_chunk, void* workspace, size_t workspace_bytes);
 
+/*
+ * lp_bwd on one rank of a vocabulary mesh, with the sum of the dH partials over the mesh's
+ * shards (the psum of the bf16 hidden cotangent, the transpose of losses.py:253-259) done
+ * inside the dH GEMM over NVLink: each rank stores its bf16 partial tiles into its own copy
+ * of a symmetric buffer and counts them on per-row-block counters in every rank's copy
+ * (multimem.red); reduce items of the same persistent launch then sum rank r's share of each
+ * finished row block across all copies through the NVSwitch (multimem.ld_reduce, f32
+ * accumulation) and store the result to every copy (multimem.st). On return (stream order)
+ * every rank's dH copy holds the sum once all ranks have passed the next lp_peer_barrier.
+ *   dH / dH_multicast   this rank's address and the multicast address of a bf16 [T, ld_dh]
+ *                       buffer bound on every rank (NVLS multicast object); 16-B aligned
+ *   counters / counters_multicast  u32 [lp_bwd_sum_counters(T)] in the same kind of memory,
+ *                       zeroed on every rank before the lp_peer_barrier preceding the call
+ *   rank, world         this rank's position in the mesh and the mesh size
+ *   timeout_ms          bound of every wait for the other ranks' tiles (device error on expiry)
+ * Other arguments as lp_bwd (dH is always bf16; LP_BWD_DH_F32 / LP_BWD_NO_DH are rejected).
+ * The workspace is lp_bwd_workspace_bytes(T, d, Vs, token_chunk, flags).
+ */
+LP_API size_t lp_bwd_sum_counters(int64_t T);
+LP_API int lp_bwd_sum(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs,
+                      int64_t v_off, const int32_t* y, float softcap, const float* norm, const float* g, void* dH,
+                      void* dH_multicast, int64_t ld_dh, unsigned* counters, unsigned* counters_multicast, int rank,
+                      int world, int timeout_ms, void* dW, int flags, int64_t token_chunk, void* workspace,
+                      size_t workspace_bytes);
+
 /* Scratch bytes lp_compact needs for B * N response slots. */
 LP_API size_t lp_compact_workspace_bytes(int64_t B, int64_t N);
 
@@ -195,6 +220,20 @@ LP_API int lp_compact(void* stream, const uint8_t* mask, int64_t B, int64_t N, c
 LP_API int lp_scatter_rows(void* stream, const void* src, int64_t src_stride, const int32_t* pos, int64_t slots,
                     int64_t width, int elem_bytes, void* out, int64_t out_stride, int64_t rows_per_group,
                     int64_t group_stride, int out_elem_bytes);
+
+/*
+ * Device-side barrier of the `world` ranks of a vocabulary mesh, on `stream` (one small
+ * kernel). It brackets lp_bwd_sum: one barrier before it (every rank has zeroed its
+ * counters and finished reading its previous dH), one after it (every rank's multicast
+ * stores have landed).
+ *   signal_pads  device array [world] of u64: this process's address of each rank's
+ *                signal pad (peer-mapped memory, u32 slots, zero-initialised)
+ *   channel      slot row used: slots [channel * world, (channel + 1) * world) of each pad
+ *   timeout_ms   bound of every wait; on expiry the kernel records a device error
+ *                (lp_device_error) and returns instead of hanging
+ */
+LP_API int lp_peer_barrier(void* stream, const unsigned long long* signal_pads, int rank, int world, int channel,
+                           int timeout_ms);
 
 /*
  * Test hook of the tensor-core core (no reference counterpart): D[M, N] = A . B^T in f32,

@@ -19,7 +19,7 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
-from gemma4_posttrain_jax_b200 import completion_logps, make_mesh, per_token_logps, shard_rows  # noqa: E402
+from gemma4_posttrain_jax_b200 import completion_logps, make_mesh, per_token_logps, shard_rows, sharding  # noqa: E402
 from oracle import logprob_oracle as orc  # noqa: E402
 
 
@@ -27,40 +27,64 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / np.linalg.norm(b))
 
 
-def main() -> int:
-    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    mesh = make_mesh()
-    rng = np.random.default_rng(20260925)
-    V, T, d = 1024 * world + 0, 777, 160
+def check_per_token(mesh, dev, rank, world, mode, V, T, d, seed) -> bool:
+    """per_token_logps fwd + bwd on the mesh with the dH sum done by `mode`; rank 0 checks."""
+    os.environ["LP_B200_DH_REDUCE"] = mode
+    rng = np.random.default_rng(seed)
     w = orc.bf16_round(rng.normal(size=(V, d)) * 1.5)
     h = orc.bf16_round(rng.normal(size=(T, d)))
     y = rng.integers(0, V, size=T).astype(np.int32)
     y[:4] = [0, V // world - 1, V // world, V - 1]
     g = rng.normal(size=T).astype(np.float32)
+    g[5:40] = 0.0  # rows the backward skips
     W = shard_rows(torch.from_numpy(w), mesh).to(dev).to(torch.bfloat16).requires_grad_(True)
     H = torch.from_numpy(h).to(dev).to(torch.bfloat16).requires_grad_(True)
-    lp = per_token_logps(W, H, torch.from_numpy(y).to(dev), softcap=30.0, mesh=mesh)
-    (lp * torch.from_numpy(g).to(dev)).sum().backward()
-    dW_parts = [torch.empty_like(W.grad) for _ in range(world)]
-    dist.all_gather(dW_parts, W.grad)
     ok = True
-    if rank == 0:
-        lp_ref, dW_ref, dH_ref = orc.logps_grads_f64(w, h, y, g, 30.0)
-        e_lp = float(np.abs(lp.detach().cpu().numpy() - lp_ref).max())
-        e_h = rel_l2(H.grad.float().cpu().numpy(), dH_ref)
-        e_w = rel_l2(torch.cat(dW_parts).float().cpu().numpy(), dW_ref)
-        print(f"world={world}: logp max abs {e_lp:.2e}, dH rel-L2 {e_h:.2e}, dW rel-L2 {e_w:.2e}", flush=True)
-        ok = e_lp <= 2e-3 and e_h <= 1e-2 and e_w <= 1e-2
+    for _ in range(2):  # the second pass reuses the (re-zeroed) multicast buffer
+        W.grad = H.grad = None
+        lp = per_token_logps(W, H, torch.from_numpy(y).to(dev), softcap=30.0, mesh=mesh)
+        (lp * torch.from_numpy(g).to(dev)).sum().backward()
+        dW_parts = [torch.empty_like(W.grad) for _ in range(world)]
+        dist.all_gather(dW_parts, W.grad)
+        used = sharding.dh_reduce_mode(mesh)
+        if mode == "multimem" and used == "multimem" and not sharding._DH_BUFFERS:
+            used = "nccl (no NVLS multicast on this system)"
+        if rank == 0:
+            lp_ref, dW_ref, dH_ref = orc.logps_grads_f64(w, h, y, g, 30.0)
+            e_lp = float(np.abs(lp.detach().cpu().numpy() - lp_ref).max())
+            e_h = rel_l2(H.grad.float().cpu().numpy(), dH_ref)
+            e_w = rel_l2(torch.cat(dW_parts).float().cpu().numpy(), dW_ref)
+            zero_rows = bool((H.grad[5:40] == 0).all())
+            print(f"world={world} T={T} d={d} dH sum={used}: logp max abs {e_lp:.2e}, dH rel-L2 {e_h:.2e}, "
+                  f"dW rel-L2 {e_w:.2e}, skipped rows zero: {zero_rows}", flush=True)
+            ok = ok and e_lp <= 2e-3 and e_h <= 1e-2 and e_w <= 1e-2 and zero_rows
+    return ok
+
+
+def main() -> int:
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    os.environ.setdefault("LP_B200_PEER_TIMEOUT_MS", "10000")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    mesh = make_mesh()
+    ok = True
+    for mode in ("multimem", "nccl"):
+        ok = check_per_token(mesh, dev, rank, world, mode, 1024 * world, 777, 160, 20260925) and ok
+    # several M / N tiles, split K over the vocabulary shard, ragged edges
+    ok = check_per_token(mesh, dev, rank, world, "multimem", 8192 * world, 2100, 392, 7) and ok
+    os.environ["LP_B200_DH_REDUCE"] = "multimem"
+    rng = np.random.default_rng(20260926)
+    V, d = 1024 * world, 160
+    w = orc.bf16_round(rng.normal(size=(V, d)) * 1.5)
+    W = shard_rows(torch.from_numpy(w), mesh).to(dev).to(torch.bfloat16)
     # GRPO caller, response slots compacted, same mesh
     B, Pw, N = 3, 5, 40
     hid = orc.bf16_round(rng.normal(size=(B, Pw + N, d)))
     ids = rng.integers(0, V, size=(B, N)).astype(np.int32)
     mask = np.arange(N)[None, :] < np.array([40, 7, 0])[:, None]
     Hd = torch.from_numpy(hid).to(dev).to(torch.bfloat16).requires_grad_(True)
-    out = completion_logps(W.detach(), Hd, torch.from_numpy(ids).to(dev), torch.from_numpy(mask).to(dev),
+    out = completion_logps(W, Hd, torch.from_numpy(ids).to(dev), torch.from_numpy(mask).to(dev),
                            prompt_width=Pw, softcap=30.0, mesh=mesh)
     out.sum().backward()
     if rank == 0:
@@ -71,6 +95,13 @@ def main() -> int:
         print(f"world={world}: completion logp max abs {e2:.2e}, invalid slots zero: {(got[~mask] == 0).all()}",
               flush=True)
         ok = ok and e2 <= 2e-3 and bool((got[~mask] == 0).all())
+        bi, ji = np.nonzero(mask)
+        _, _, dHr = orc.logps_grads_f64(w, resp[bi, ji], ids[bi, ji], np.ones(len(bi), np.float32), 30.0)
+        ref_dh = np.zeros(hid.shape)
+        ref_dh[bi, Pw - 1 + ji] = dHr
+        e3 = rel_l2(Hd.grad.float().cpu().numpy(), ref_dh)
+        print(f"world={world}: completion dH rel-L2 {e3:.2e}", flush=True)
+        ok = ok and e3 <= 1e-2
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.broadcast(flag, 0)
     dist.destroy_process_group()

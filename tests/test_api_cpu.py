@@ -78,3 +78,14 @@ def test_native_metadata_is_empty_and_unknown_rejected():
     assert proto.logprob_run_metadata("pallas")["logprob_protocol"] == proto.PALLAS_LOGPROB_PROTOCOL
     with pytest.raises(ValueError, match="unknown logprob"):
         proto.logprob_run_metadata("unknown")
+
+
+def test_dh_reduce_mode_single_shard_and_override(monkeypatch):
+    from gemma4_posttrain_jax_b200 import sharding
+
+    assert sharding.dh_reduce_mode(None) == "none"
+    assert sharding.dh_reduce_mode(sharding.make_mesh()) == "none"  # no process group: one shard
+    monkeypatch.setenv("LP_B200_PEER_TIMEOUT_MS", "250")
+    assert sharding.peer_timeout_ms() == 250
+    monkeypatch.setenv("LP_B200_PEER_TIMEOUT_MS", "0")
+    assert sharding.peer_timeout_ms() == 1

@@ -39,6 +39,8 @@ def _vocab_parallel_worker(rank, world, port, q):
             all_gather_rows,
             all_gather_stats,
             all_reduce_sum,
+            dh_reduce_mode,
+            dh_sum_buffer,
             make_mesh,
             reduce_scatter_rows,
             shard_rows,
@@ -72,6 +74,9 @@ def _vocab_parallel_worker(rank, world, port, q):
         full = all_gather_rows(rows, mesh)
         back = reduce_scatter_rows(full.clone(), mesh)
         summed = all_reduce_sum(torch.ones(5) * (rank + 1), mesh)
+        # a gloo mesh sums dH with a collective after the GEMM: no multicast buffer is made
+        assert dh_reduce_mode(mesh) == "nccl"
+        assert dh_sum_buffer(mesh, 16, 8, torch.device("cpu")) is None
         q.put((rank, err, full[:, 0].tolist(), back[:, 0].tolist(), summed[0].item()))
         dist.destroy_process_group()
     except Exception as exc:  # noqa: BLE001
