@@ -48,6 +48,11 @@ _SIG = {
     "lp_fwd": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, ctypes.c_float, _P, _P, _P, ctypes.c_size_t]),
     "lp_fwd_noalloc": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, ctypes.c_float, _P, _P]),
     "lp_combine": (ctypes.c_int, [_P, _P, ctypes.c_int, _I64, _P, _P]),
+    "lp_fwd_sum": (
+        ctypes.c_int,
+        [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, ctypes.c_float, _P, _P, _I64, _P, _P, _P, ctypes.c_uint,
+         ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_size_t],
+    ),
     "lp_bwd_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, ctypes.c_int]),
     "lp_bwd": (
         ctypes.c_int,

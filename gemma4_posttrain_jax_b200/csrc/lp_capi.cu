@@ -655,6 +655,61 @@ int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
   return LP_OK;
 }
 
+int lp_fwd_sum(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs,
+               int64_t v_off, const int32_t* y, float softcap, void* exchange, void* exchange_multicast,
+               int64_t ld_exchange, unsigned* counter, unsigned* counter_multicast, unsigned* arrivals,
+               unsigned epoch, int rank, int world, int timeout_ms, float* logp, float* norm, void* workspace,
+               size_t workspace_bytes) {
+  int rc = check_common(H, T, d, ldh, W, Vs, y);
+  if (rc) return rc;
+  if (world < 1 || rank < 0 || rank >= world) return fail(LP_EINVAL, "bad rank %d / world %d", rank, world);
+  if (exchange == nullptr || exchange_multicast == nullptr || counter == nullptr || counter_multicast == nullptr ||
+      arrivals == nullptr)
+    return fail(LP_EINVAL, "null exchange buffer, counter or arrival counter");
+  if (((reinterpret_cast<uintptr_t>(exchange) | reinterpret_cast<uintptr_t>(exchange_multicast)) & 15) != 0)
+    return fail(LP_EINVAL, "the exchange buffer and its multicast address must be 16-byte aligned");
+  if (ld_exchange < T) return fail(LP_EINVAL, "ld_exchange=%lld < T=%lld", (long long)ld_exchange, (long long)T);
+  if (epoch == 0 || (unsigned long long)epoch * (unsigned)world > 0xffffffffull)
+    return fail(LP_EINVAL, "epoch %u out of range for world %d", epoch, world);
+  if (timeout_ms <= 0) return fail(LP_EINVAL, "timeout_ms must be positive");
+  if (T == 0) return LP_OK;
+  if (logp == nullptr && norm == nullptr) return fail(LP_EINVAL, "null logp and norm");
+  DeviceInfo* di = nullptr;
+  if ((rc = current_device_info(&di))) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int cg = cta_group_for(CG_FWD);
+  GemmSched s = plan_fwd(T, Vs, d, workers(di, cg), 128 * cg);
+  const size_t part_bytes = align_up((size_t)2 * s.n_groups * T * sizeof(float2), 256);
+  const size_t need = part_bytes + align_up((size_t)T * 4, 256);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(LP_EWORKSPACE, "lp_fwd_sum needs %zu workspace bytes, got %zu", need, workspace_bytes);
+  float2* part = reinterpret_cast<float2*>(workspace);
+  float* tgt = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + part_bytes);
+
+  alignas(64) CUtensorMap ta, tb;
+  if ((rc = map_bf16(&ta, H, d, T, ldh, BK, 128, "hidden"))) return rc;
+  if ((rc = map_bf16(&tb, W, d, Vs, d, BK, b_box_rows(cg), "embedding"))) return rc;
+  GemmParams p{};
+  p.s = s;
+  p.e.y = y;
+  p.e.v_off = v_off;
+  p.e.softcap = softcap;
+  p.e.part = part;
+  p.e.tgt = tgt;
+  set_hints(p, G_FWD);
+  if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di, "fwd_lse_gemm"))) return rc;
+  // one block per SM at most: every block must be resident while the blocks wait for the
+  // other ranks
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(T, 256), di->sms);
+  ProfScope prof(st, "fwd_finalize_mesh");
+  fwd_finalize_mesh_kernel<<<grid, 256, 0, st>>>(
+      part, 2 * s.n_groups, (int)T, tgt, y, v_off, Vs, reinterpret_cast<float4*>(exchange_multicast),
+      reinterpret_cast<const float4*>(exchange), ld_exchange, counter_multicast, counter, arrivals,
+      epoch * (unsigned)world, rank, world, (unsigned long long)timeout_ms * 1000000ull, logp, norm);
+  LP_LAUNCH_CHECK("fwd_finalize_mesh_kernel");
+  return LP_OK;
+}
+
 int lp_combine(void* stream, const float* shard_stats, int P, int64_t T, float* logp, float* norm) {
   if (P <= 0 || T < 0) return fail(LP_EINVAL, "bad P=%d or T=%lld", P, (long long)T);
   if (T == 0) return LP_OK;

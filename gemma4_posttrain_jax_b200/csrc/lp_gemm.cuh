@@ -432,14 +432,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+          // Peek at the next stage's barrier (non-blocking) before issuing this stage's MMAs,
+          // so a stage that has already landed costs no blocking wait.
+          bool ready = mbar_test_wait(&full_bar[it % NS], (it / NS) & 1);
           for (int kb = 0; kb < un.kb_count; ++kb, ++it) {
             const int s = it % NS;
             const uint32_t ph = (it / NS) & 1;
             const unsigned long long w1 = P.dbg ? clk64() : 0ull;
-            if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, DEV_TIMEOUT_MMA)) {
+            if (!ready && !mbar_wait_bounded(&full_bar[s], ph, abort_flag, DEV_TIMEOUT_MMA)) {
               ok = false;
               break;
             }
+            ready = kb + 1 < un.kb_count && mbar_test_wait(&full_bar[(it + 1) % NS], ((it + 1) / NS) & 1);
             if (P.dbg) {
               dbg_full += clk64() - w1;
               dbg_kb += 1;

@@ -73,6 +73,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of the phase of `parity` (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase of `parity` to complete. Returns false (and raises *abort) when the
 // CTA is already aborting or when the wait exceeds kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
@@ -322,6 +335,13 @@ __device__ __forceinline__ uint4 multimem_ld_reduce_bf16x8(const void* mc) {
 __device__ __forceinline__ void multimem_st_bf16x8(void* mc, uint4 v) {
   asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Stores 16 bytes (four f32) to every copy of a multicast-bound buffer.
+__device__ __forceinline__ void multimem_st_f32x4(void* mc, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
                : "memory");
 }
 

@@ -33,6 +33,90 @@ __global__ void fwd_finalize_kernel(const float2* __restrict__ part, int n_group
   if (logp != nullptr) logp[t] = tgt - (mx + logf(s));
 }
 
+// Per-row (max, sum, owned target) of this shard from the forward GEMM's partials.
+__device__ __forceinline__ float3 shard_triple(const float2* __restrict__ part, int n_groups, int T, int t,
+                                               const float* __restrict__ tgt_ws, const int32_t* __restrict__ y,
+                                               long long v_off, long long Vs) {
+  float m = -INFINITY;
+  for (int g = 0; g < n_groups; ++g) m = fmaxf(m, part[(size_t)g * T + t].x);
+  float s = 0.f;
+  for (int g = 0; g < n_groups; ++g) {
+    const float2 p = part[(size_t)g * T + t];
+    s += p.y * exp2f(p.x - m);
+  }
+  const long long local = (long long)y[t] - v_off;
+  const bool owned = local >= 0 && local < Vs;
+  return make_float3(m * kLn2, s, owned ? tgt_ws[t] : 0.f);
+}
+
+// The forward's finalize on one rank of a vocabulary mesh, fused with the exchange of the
+// per-shard triples over NVLink (the pmax / psum of losses.py:219,243-245):
+//   1. every thread merges its rows' partials into this shard's (max, sum, owned target)
+//      and stores them, as one 16-byte multimem store, into slot `rank` of every rank's
+//      copy of the exchange buffer [world][ld] (f32x4);
+//   2. the last block of this launch to finish step 1 (an arrival counter in this GPU's
+//      memory) adds 1 to the exchange counter in every copy (release at system scope);
+//   3. every block waits (bounded) until its local copy of the counter reaches `target`
+//      (epoch * world: all ranks have stored), then merges the `world` triples of its rows
+//      exactly as combine_kernel does: logp = tgt - m - log s, norm = (m, s).
+// All blocks of the grid must be resident at once (the host keeps the grid at or below the
+// SM count), since a block only waits after its own stores.
+__global__ void fwd_finalize_mesh_kernel(const float2* __restrict__ part, int n_groups, int T,
+                                         const float* __restrict__ tgt_ws, const int32_t* __restrict__ y,
+                                         long long v_off, long long Vs, float4* xch_mc, const float4* xch_local,
+                                         long long ld, unsigned* cnt_mc, const unsigned* cnt_local, unsigned* arrivals,
+                                         unsigned target, int rank, int world, unsigned long long limit_ns,
+                                         float* __restrict__ logp, float* __restrict__ norm) {
+  __shared__ int s_go;
+  const int stride = gridDim.x * blockDim.x;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += stride) {
+    const float3 v = shard_triple(part, n_groups, T, t, tgt_ws, y, v_off, Vs);
+    multimem_st_f32x4(xch_mc + (size_t)rank * ld + t, make_float4(v.x, v.y, v.z, 0.f));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // this block's multicast stores before its arrival
+    const unsigned prev = atomicAdd(arrivals, 1u);
+    if (prev == gridDim.x - 1) {
+      // every block has arrived: reset the arrival counter for the next call, then count
+      // this rank once in every copy of the exchange counter
+      *arrivals = 0u;
+      __threadfence_system();
+      multimem_red_add_release_u32(cnt_mc, 1u);
+    }
+    int go = 1;
+    if (ld_acquire_sys_u32(cnt_local) < target) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys_u32(cnt_local) < target) {
+        if (globaltimer_ns() - t0 > limit_ns) {
+          record_device_error(DEV_TIMEOUT_PEER);
+          go = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    s_go = go;
+  }
+  __syncthreads();
+  if (!s_go) return;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += stride) {
+    float m = -INFINITY;
+    for (int p = 0; p < world; ++p) m = fmaxf(m, __ldcg(&xch_local[(size_t)p * ld + t]).x);
+    float s = 0.f, tgt = 0.f;
+    for (int p = 0; p < world; ++p) {
+      const float4 v = __ldcg(&xch_local[(size_t)p * ld + t]);
+      s += v.y * expf(v.x - m);
+      tgt += v.z;
+    }
+    if (logp != nullptr) logp[t] = tgt - m - logf(s);
+    if (norm != nullptr) {
+      norm[t] = m;
+      norm[(size_t)T + t] = s;
+    }
+  }
+}
+
 // Cross-shard combine: global max, rescaled sum, summed owned target logit.
 __global__ void combine_kernel(const float* __restrict__ shard_stats, int P, int T, float* __restrict__ logp,
                                float* __restrict__ norm) {

@@ -3,9 +3,9 @@
 ``per_token_logps`` keeps the signature, argument meaning and error behaviour of
 ``gemma4_posttrain_jax/losses.py:307-343`` and adds ``backend="cuda"``: a
 ``torch.autograd.Function`` (the analogue of the reference's ``jax.custom_vjp``,
-``pallas/lm_head_logprob_tpuv4.py:69-94``) whose forward runs ``lp_fwd`` (+ the NCCL
-all-gather and ``lp_combine`` when the vocabulary is sharded) and whose backward runs
-``lp_bwd`` (+ the dH sum over shards). The callers on the path are mirrored too:
+``pallas/lm_head_logprob_tpuv4.py:69-94``) whose forward runs ``lp_fwd`` (``lp_fwd_sum``,
+or NCCL all-gather + ``lp_combine``, when the vocabulary is sharded) and whose backward
+runs ``lp_bwd`` (+ the dH sum over shards). The callers on the path are mirrored too:
 ``sft_token_logps`` (the shift of ``losses.py:910-926``) and ``completion_logps`` (the
 response slice of ``losses.py:667-682``, with the padded slots compacted away).
 
@@ -20,7 +20,15 @@ import torch
 
 from . import ops
 from .phase_timer import phase
-from .sharding import VocabMesh, all_gather_stats, all_reduce_sum, dh_sum_buffer, peer_timeout_ms, vocab_offset
+from .sharding import (
+    VocabMesh,
+    all_gather_stats,
+    all_reduce_sum,
+    dh_sum_buffer,
+    peer_timeout_ms,
+    stats_exchange,
+    vocab_offset,
+)
 
 
 # A backward skips the rows whose upstream gradient is exactly zero (they add nothing to dH
@@ -98,6 +106,19 @@ def _backward_rows(embed, H, y, softcap, norm, g, *, mesh, vocab_offset, need_dh
     return dH, dW, pos, False
 
 
+def _mesh_forward(embed, H, y, softcap, mesh, off):
+    """Global (logp, normalization) of rows H over the vocabulary mesh: the pmax / psum
+    combine of ``losses.py:219,243-245``, exchanged over NVLink inside the forward
+    (``lp_fwd_sum``) where the mesh has a multicast buffer, else NCCL all-gather + combine."""
+    xch = stats_exchange(mesh, H.shape[0], H.device)
+    if xch is not None:
+        return ops.shard_forward_sum(embed, H, y, softcap, xch, vocab_offset=off, timeout_ms=peer_timeout_ms())
+    stats, _ = ops.shard_forward(embed, H, y, softcap, vocab_offset=off, want_logp=False)
+    with phase("stats_all_gather"):
+        gathered = all_gather_stats(stats, mesh)
+    return ops.combine(gathered)
+
+
 def _validate(embed: torch.Tensor, hidden: torch.Tensor, targets: torch.Tensor, vocab_chunk: int, sequence_chunk: int):
     """The three argument checks of ``losses.py:281-286``, same messages."""
     if tuple(hidden.shape[:-1]) != tuple(targets.shape):
@@ -122,10 +143,7 @@ class _CudaTokenLogps(torch.autograd.Function):
         P = mesh.size if mesh is not None else 1
         if P > 1:
             off = vocab_offset(embed.shape[0], mesh)
-            stats, _ = ops.shard_forward(embed, hidden2d, targets1d, softcap, vocab_offset=off, want_logp=False)
-            with phase("stats_all_gather"):
-                gathered = all_gather_stats(stats, mesh)
-            logp, norm = ops.combine(gathered)
+            logp, norm = _mesh_forward(embed, hidden2d, targets1d, softcap, mesh, off)
         else:
             off = 0
             stats, logp = ops.shard_forward(embed, hidden2d, targets1d, softcap, want_logp=True)
@@ -242,10 +260,7 @@ class _CompletionLogps(torch.autograd.Function):
         off = vocab_offset(embed.shape[0], mesh) if P > 1 else 0
         if n > 0:
             if P > 1:
-                stats, _ = ops.shard_forward(embed, Hn, yn, softcap, vocab_offset=off, want_logp=False)
-                with phase("stats_all_gather"):
-                    gathered = all_gather_stats(stats, mesh)
-                logp_c, norm = ops.combine(gathered)
+                logp_c, norm = _mesh_forward(embed, Hn, yn, softcap, mesh, off)
             else:
                 stats, logp_c = ops.shard_forward(embed, Hn, yn, softcap, want_logp=True)
                 norm = stats[:2]

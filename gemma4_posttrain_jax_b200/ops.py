@@ -98,6 +98,46 @@ def shard_forward(
     return stats, logp
 
 
+def shard_forward_sum(
+    embed: torch.Tensor,
+    hidden: torch.Tensor,
+    targets: torch.Tensor,
+    softcap: float | None,
+    exchange,
+    *,
+    vocab_offset: int,
+    timeout_ms: int,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``lp_fwd_sum``: the forward of this rank's shard with the triples exchanged over
+    NVLink (``exchange`` is a ``sharding.StatsExchange`` with room for T rows; every rank of
+    the mesh makes the same call). Returns the global (logp [T], normalization [2, T])."""
+    dev = _require_cuda(embed, hidden, targets)
+    _check_bf16("embedding", embed)
+    _check_bf16("hidden", hidden)
+    lib = _lib.load()
+    h2, ldh = _rows(hidden)
+    T, d = h2.shape
+    Vs = embed.shape[0]
+    if T > exchange.rows:
+        raise ValueError(f"stats exchange holds {exchange.rows} rows, {T} needed")
+    w = embed if embed.is_contiguous() else embed.contiguous()
+    y = targets.reshape(-1).to(torch.int32).contiguous()
+    logp = torch.empty((T,), dtype=torch.float32, device=dev)
+    norm = torch.empty((2, T), dtype=torch.float32, device=dev)
+    if T == 0:
+        return logp, norm
+    ws, wsp, wsn = _workspace(lib.lp_fwd_workspace_bytes(T, Vs), dev)
+    cap = float(softcap) if softcap is not None else 0.0
+    xch, xch_mc, cnt, cnt_mc, arr, epoch = exchange.next_call()
+    rc = lib.lp_fwd_sum(
+        _stream(dev), _ptr(h2), T, d, ldh, _ptr(w), Vs, int(vocab_offset), _ptr(y), cap, ctypes.c_void_p(xch),
+        ctypes.c_void_p(xch_mc), exchange.rows, ctypes.c_void_p(cnt), ctypes.c_void_p(cnt_mc), ctypes.c_void_p(arr),
+        epoch, exchange.rank, exchange.world, int(timeout_ms), _ptr(logp), _ptr(norm), wsp, wsn,
+    )
+    _lib.check(rc, "lp_fwd_sum")
+    return logp, norm
+
+
 def combine(shard_stats: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """``lp_combine``: [P, 3, T] per-shard triples -> (logp [T], normalization [2, T])."""
     dev = _require_cuda(shard_stats)

@@ -8,7 +8,9 @@ embedding to ``P("d", None)``), replicates hidden states and targets at the
 mesh axis is a process group, the shard is the local row block, and the exchanges are
 NCCL collectives (gloo on CPU for the host-logic tests):
 
-  * all-gather of the per-shard (max, sum, owned target logit) triples, 12 bytes/token,
+  * exchange of the per-shard (max, sum, owned target logit) triples, 12 bytes/token:
+    inside the forward's finalize kernel through an NVLS multicast buffer
+    (``StatsExchange``, ``lp_fwd_sum``) where the GPUs support it, else an NCCL all-gather
     merged on the device by ``lp_combine``;
   * sum of the per-shard dH partials: inside the dH GEMM through an NVLS multicast buffer
     (``DhSumBuffer``, multimem reductions from the GEMM epilogue) where the GPUs support
@@ -211,4 +213,82 @@ def dh_sum_buffer(mesh: VocabMesh, rows: int, d: int, device: torch.device) -> D
             _MULTICAST_UNAVAILABLE.add(gkey)
             return None
         _DH_BUFFERS[key] = buf
+    return buf
+
+
+# ----------------------------------------------------------------------------- multicast stats exchange
+_STATS_EXCHANGES: dict[tuple, "StatsExchange"] = {}
+
+
+def stats_exchange_mode(mesh: VocabMesh | None) -> str:
+    """How the per-shard triples are exchanged: "none" (one shard), "multimem" (inside the
+    forward's finalize kernel over NVLS multicast) or "nccl" (all-gather + ``lp_combine``).
+    ``LP_B200_STATS_EXCHANGE=nccl`` forces the all-gather."""
+    if mesh is None or mesh.size == 1:
+        return "none"
+    if os.environ.get("LP_B200_STATS_EXCHANGE", "multimem") != "multimem" or not _is_nccl(mesh):
+        return "nccl"
+    return "multimem"
+
+
+class StatsExchange:
+    """Symmetric memory bound to an NVLS multicast object on every rank of the mesh: two
+    f32x4 [world, rows] exchange buffers, one u32 exchange counter each and a local arrival
+    counter, the operands of ``lp_fwd_sum``. Calls alternate between the two buffers, and
+    call number k of a buffer waits for counter == k * world, so the counters are never
+    reset and no barrier is needed between calls (the pmax / psum of
+    ``losses.py:219,243-245`` as one NVLink exchange inside the forward)."""
+
+    def __init__(self, mesh: VocabMesh, rows: int, device: torch.device):
+        import torch.distributed._symmetric_memory as symm_mem  # noqa: PLC0415 - CUDA + NCCL only
+
+        group = mesh.group if mesh.group is not None else dist.group.WORLD
+        self.rows, self.device = int(rows), device
+        world = mesh.size
+        slot_bytes = -(-world * self.rows * 16 // 4096) * 4096
+        self.slot_bytes = slot_bytes
+        total = 2 * slot_bytes + 4096  # two exchange buffers + counters (128 B apart) + arrivals
+        self.storage = symm_mem.empty((total,), dtype=torch.uint8, device=device)
+        self.storage[2 * slot_bytes :].zero_()
+        torch.cuda.synchronize(device)  # counters are zero on every rank before any rank signals
+        self.handle = symm_mem.rendezvous(self.storage, group)
+        mc = int(self.handle.multicast_ptr)
+        if mc == 0:
+            raise RuntimeError("symmetric memory has no multicast mapping on this system")
+        self.base, self.base_mc = int(self.storage.data_ptr()), mc
+        self.rank, self.world = int(self.handle.rank), int(self.handle.world_size)
+        self.calls = 0
+
+    def next_call(self) -> tuple[int, int, int, int, int, int]:
+        """(exchange, exchange_mc, counter, counter_mc, arrivals, epoch) of the next call."""
+        k = self.calls
+        self.calls += 1
+        slot, epoch = k % 2, k // 2 + 1
+        cnt = 2 * self.slot_bytes + 128 * slot
+        arrivals = 2 * self.slot_bytes + 256
+        return (self.base + slot * self.slot_bytes, self.base_mc + slot * self.slot_bytes, self.base + cnt,
+                self.base_mc + cnt, self.base + arrivals, epoch)
+
+
+def stats_exchange(mesh: VocabMesh, rows: int, device: torch.device) -> StatsExchange | None:
+    """The mesh's multicast stats exchange with room for ``rows`` tokens (collective when it
+    has to grow: every rank holds the same token count because hidden states and targets
+    are replicated), or None where the multicast path is off or unavailable."""
+    if stats_exchange_mode(mesh) != "multimem":
+        return None
+    gkey = (id(mesh.group), device.index)
+    if gkey in _MULTICAST_UNAVAILABLE:
+        return None
+    buf = _STATS_EXCHANGES.get(gkey)
+    if buf is None or buf.rows < rows:
+        grow = max(int(rows), -(-int(rows * 5 // 4) // 1024) * 1024)
+        if buf is not None:
+            torch.cuda.synchronize(device)  # the old buffer's last exchange has finished here
+        _STATS_EXCHANGES.pop(gkey, None)
+        try:
+            buf = StatsExchange(mesh, grow, device)
+        except (RuntimeError, ImportError):
+            _MULTICAST_UNAVAILABLE.add(gkey)
+            return None
+        _STATS_EXCHANGES[gkey] = buf
     return buf

@@ -14,7 +14,8 @@
  *                                               custom_vjp fwd / bwd and the dW kernel
  * Vocabulary parallelism: each caller process holds one shard W[v_off : v_off + Vs] and
  * calls lp_fwd on it; the per-shard (max, sum, owned target logit) triples are exchanged
- * by the caller's collective (NCCL all-gather) and merged by lp_combine.
+ * by the caller's collective (NCCL all-gather) and merged by lp_combine, or exchanged over
+ * NVLink inside the forward by lp_fwd_sum where the GPUs share an NVSwitch multicast.
  *
  * Conventions
  *   - All pointers are device pointers unless stated. `stream` is a cudaStream_t (NULL =
@@ -145,6 +146,34 @@ LP_API int lp_fwd_noalloc(void* stream, const void* H, int64_t T, int64_t d, int
  *               reference's `normalization` output (losses.py:246-247)
  */
 LP_API int lp_combine(void* stream, const float* shard_stats, int P, int64_t T, float* logp, float* norm);
+
+/*
+ * lp_fwd on one rank of a vocabulary mesh with the exchange of the per-shard triples done
+ * over NVLink inside the forward's finalize kernel: the pmax / psum combine of
+ * losses.py:219,243-245 without a separate collective (it replaces lp_fwd + an all-gather
+ * + lp_combine, with the same floats as that sequence). Each rank stores its rows'
+ * (max, sum, owned target logit) into its slot of every rank's copy of a symmetric
+ * exchange buffer (NVLS multicast store), counts itself once on an exchange counter in
+ * every copy, waits until all `world` ranks have done so and merges the slots locally.
+ *   exchange / exchange_multicast  this rank's address and the multicast address of an f32x4
+ *                     [world, ld_exchange] buffer bound on every rank (16-byte aligned)
+ *   counter / counter_multicast    one u32 in the same kind of memory, zero when the buffer
+ *                     was set up; never reset: call number `epoch` (1, 2, ...) of this
+ *                     (exchange, counter) pair waits for epoch * world
+ *   arrivals          one u32 in this GPU's memory, zero before the first call (each call
+ *                     leaves it zero)
+ *   logp / norm       f32 [T] global target logp / f32 [2, T] global (max, sum), as lp_combine
+ *   timeout_ms        bound of the wait for the other ranks (device error on expiry)
+ * Every rank makes the same calls in the same order, stream-ordered on each rank, and
+ * consecutive calls alternate between two (exchange, counter) pairs: a rank overwrites a
+ * slot only after the call with the other pair has seen every rank finish reading it.
+ * The workspace is lp_fwd_workspace_bytes(T, Vs).
+ */
+LP_API int lp_fwd_sum(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs,
+                      int64_t v_off, const int32_t* y, float softcap, void* exchange, void* exchange_multicast,
+                      int64_t ld_exchange, unsigned* counter, unsigned* counter_multicast, unsigned* arrivals,
+                      unsigned epoch, int rank, int world, int timeout_ms, float* logp, float* norm, void* workspace,
+                      size_t workspace_bytes);
 
 /* Scratch bytes lp_bwd needs; token_chunk <= 0 selects the default chunk. */
 LP_API size_t lp_bwd_workspace_bytes(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int flags);

@@ -27,9 +27,14 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / np.linalg.norm(b))
 
 
-def check_per_token(mesh, dev, rank, world, mode, V, T, d, seed) -> bool:
-    """per_token_logps fwd + bwd on the mesh with the dH sum done by `mode`; rank 0 checks."""
+LOGPS: dict = {}
+
+
+def check_per_token(mesh, dev, rank, world, mode, V, T, d, seed, stats_mode="multimem") -> bool:
+    """per_token_logps fwd + bwd on the mesh with the dH sum done by `mode` and the triples
+    exchanged by `stats_mode`; rank 0 checks (logps of both exchanges must be bit-identical)."""
     os.environ["LP_B200_DH_REDUCE"] = mode
+    os.environ["LP_B200_STATS_EXCHANGE"] = stats_mode
     rng = np.random.default_rng(seed)
     w = orc.bf16_round(rng.normal(size=(V, d)) * 1.5)
     h = orc.bf16_round(rng.normal(size=(T, d)))
@@ -49,15 +54,26 @@ def check_per_token(mesh, dev, rank, world, mode, V, T, d, seed) -> bool:
         used = sharding.dh_reduce_mode(mesh)
         if mode == "multimem" and used == "multimem" and not sharding._DH_BUFFERS:
             used = "nccl (no NVLS multicast on this system)"
+        xused = sharding.stats_exchange_mode(mesh)
+        if xused == "multimem" and not sharding._STATS_EXCHANGES:
+            xused = "nccl (no NVLS multicast on this system)"
+        key = (V, T, d, seed)
+        lp_host = lp.detach().cpu().numpy()
+        same = True
+        if key in LOGPS:
+            same = bool(np.array_equal(LOGPS[key], lp_host))
+        else:
+            LOGPS[key] = lp_host
         if rank == 0:
             lp_ref, dW_ref, dH_ref = orc.logps_grads_f64(w, h, y, g, 30.0)
             e_lp = float(np.abs(lp.detach().cpu().numpy() - lp_ref).max())
             e_h = rel_l2(H.grad.float().cpu().numpy(), dH_ref)
             e_w = rel_l2(torch.cat(dW_parts).float().cpu().numpy(), dW_ref)
             zero_rows = bool((H.grad[5:40] == 0).all())
-            print(f"world={world} T={T} d={d} dH sum={used}: logp max abs {e_lp:.2e}, dH rel-L2 {e_h:.2e}, "
-                  f"dW rel-L2 {e_w:.2e}, skipped rows zero: {zero_rows}", flush=True)
-            ok = ok and e_lp <= 2e-3 and e_h <= 1e-2 and e_w <= 1e-2 and zero_rows
+            print(f"world={world} T={T} d={d} dH sum={used} stats={xused}: logp max abs {e_lp:.2e}, "
+                  f"dH rel-L2 {e_h:.2e}, dW rel-L2 {e_w:.2e}, skipped rows zero: {zero_rows}, "
+                  f"logps identical across exchanges: {same}", flush=True)
+            ok = ok and e_lp <= 2e-3 and e_h <= 1e-2 and e_w <= 1e-2 and zero_rows and same
     return ok
 
 
@@ -71,9 +87,13 @@ def main() -> int:
     ok = True
     for mode in ("multimem", "nccl"):
         ok = check_per_token(mesh, dev, rank, world, mode, 1024 * world, 777, 160, 20260925) and ok
-    # several M / N tiles, split K over the vocabulary shard, ragged edges
+    ok = check_per_token(mesh, dev, rank, world, "nccl", 1024 * world, 777, 160, 20260925, stats_mode="nccl") and ok
+    # several M / N tiles, split K over the vocabulary shard, ragged edges; the stats
+    # exchange buffer grows (a new multicast buffer) for the larger token count
     ok = check_per_token(mesh, dev, rank, world, "multimem", 8192 * world, 2100, 392, 7) and ok
+    ok = check_per_token(mesh, dev, rank, world, "multimem", 8192 * world, 2100, 392, 7, stats_mode="nccl") and ok
     os.environ["LP_B200_DH_REDUCE"] = "multimem"
+    os.environ["LP_B200_STATS_EXCHANGE"] = "multimem"
     rng = np.random.default_rng(20260926)
     V, d = 1024 * world, 160
     w = orc.bf16_round(rng.normal(size=(V, d)) * 1.5)

@@ -85,6 +85,8 @@ def test_dh_reduce_mode_single_shard_and_override(monkeypatch):
 
     assert sharding.dh_reduce_mode(None) == "none"
     assert sharding.dh_reduce_mode(sharding.make_mesh()) == "none"  # no process group: one shard
+    assert sharding.stats_exchange_mode(None) == "none"
+    assert sharding.stats_exchange_mode(sharding.make_mesh()) == "none"
     monkeypatch.setenv("LP_B200_PEER_TIMEOUT_MS", "250")
     assert sharding.peer_timeout_ms() == 250
     monkeypatch.setenv("LP_B200_PEER_TIMEOUT_MS", "0")

@@ -44,6 +44,8 @@ def _vocab_parallel_worker(rank, world, port, q):
             make_mesh,
             reduce_scatter_rows,
             shard_rows,
+            stats_exchange,
+            stats_exchange_mode,
             vocab_offset,
         )
         from oracle import logprob_oracle as orc
@@ -77,6 +79,9 @@ def _vocab_parallel_worker(rank, world, port, q):
         # a gloo mesh sums dH with a collective after the GEMM: no multicast buffer is made
         assert dh_reduce_mode(mesh) == "nccl"
         assert dh_sum_buffer(mesh, 16, 8, torch.device("cpu")) is None
+        # ... and exchanges the per-shard triples with an all-gather, not a multicast buffer
+        assert stats_exchange_mode(mesh) == "nccl"
+        assert stats_exchange(mesh, 16, torch.device("cpu")) is None
         q.put((rank, err, full[:, 0].tolist(), back[:, 0].tolist(), summed[0].item()))
         dist.destroy_process_group()
     except Exception as exc:  # noqa: BLE001
