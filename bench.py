@@ -72,6 +72,8 @@ def parse_args():
     p.add_argument("--token-chunk", type=int, default=0, help="backward token chunk (0 = library default)")
     p.add_argument("--cta-group", type=int, default=0, choices=(0, 1, 2),
                    help="tensor-core CTA group of the GEMMs (0 = library default, the CTA pair)")
+    p.add_argument("--sampler-head", type=int, default=0, metavar="B",
+                   help="instead: time the rollout sampler's LM head (lp_head) on B decode rows")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
@@ -264,11 +266,64 @@ def run_reference(args):
     return 0
 
 
+# --------------------------------------------------------------------------- sampler head
+def run_sampler_head(args):
+    """Decode-time LM head (lp_head) on B rows: greedy (no logits written) and full logits.
+
+    HBM-bound: per launch it must read W (V * d * 2 bytes) and, with logits, write B * V * 4.
+    """
+    from gemma4_posttrain_jax_b200 import _lib, ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    B = args.sampler_head
+    softcap = args.softcap if args.softcap > 0 else None
+    gen = torch.Generator(device=dev).manual_seed(SEED + 1)
+    W = (torch.randn((V, D), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    H = torch.randn((B, D), generator=gen, device=dev).to(torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > L2 between launches
+    peaks, peak_src = load_peaks()
+    out = {}
+    for mode, want in (("greedy", False), ("logits", True)):
+        for _ in range(args.warmup):
+            ops.head(W, H, softcap, want_logits=want)
+        torch.cuda.synchronize()
+        _lib.profile_enable(True)
+        for _ in range(args.steps):
+            flush.zero_()
+            ops.head(W, H, softcap, want_logits=want)
+        torch.cuda.synchronize()
+        prof = _lib.profile_read()
+        _lib.profile_enable(False)
+        ms = sum(v[0] for v in prof.values()) / args.steps
+        gemm_ms = prof["head_gemm"][0] / args.steps
+        nbytes = V * D * 2 + (B * V * 4 if want else 0)
+        out[mode] = {"ms_per_call": ms, "rows_per_s": B / (ms / 1e3), "gemm_ms": gemm_ms,
+                     "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (gemm_ms / 1e3) / 1e9,
+                     "frac_of_hbm": nbytes / (gemm_ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+    assert _lib.device_error(0) == 0
+    line = {
+        "metric": f"sampler LM head rows/s @V={V},d={D} (lp_head, {B} decode rows)",
+        "value": out["greedy"]["rows_per_s"], "unit": "rows/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": "rollout sampler head (forward_lm_head + _sample_token log-softmax / argmax)",
+                   "rows": B, "hidden": D, "vocab": V, "softcap": softcap, "l2": "flushed (256 MB) per launch"},
+        "roofline": {"bound": "hbm", "achieved": out["greedy"]["achieved_gbs"], "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": out["greedy"]["frac_of_hbm"], "peak_source": f"hbm_gbs ({peak_src})"},
+        "modes": out,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # --------------------------------------------------------------------------- CUDA arm
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.sampler_head:
+        return run_sampler_head(args)
 
     import torch.distributed as dist
 

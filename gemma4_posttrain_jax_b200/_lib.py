@@ -24,6 +24,7 @@ LP_BWD_DH_F32 = 1
 LP_BWD_DW_BF16 = 2
 LP_BWD_NO_DW = 4
 LP_BWD_NO_DH = 8
+LP_HEAD_LOGPROBS = 1
 
 # Every symbol include/lp_logprob.h declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -64,6 +65,11 @@ _SIG = {
         ctypes.c_int,
         [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, ctypes.c_float, _P, _P, _P, _P, _I64, _P, _P, ctypes.c_int,
          ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _I64, _P, ctypes.c_size_t],
+    ),
+    "lp_head_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
+    "lp_head": (
+        ctypes.c_int,
+        [_P, _P, _I64, _I64, _I64, _P, _I64, ctypes.c_float, _P, _I64, ctypes.c_int, _P, _P, _P, _P, ctypes.c_size_t],
     ),
     "lp_compact_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
     "lp_compact": (

@@ -501,6 +501,10 @@ int check_common(const void* H, int64_t T, int64_t d, int64_t ldh, const void* W
   return LP_OK;
 }
 
+// Few rows for many partials: the forward's finalize runs one block per row instead of one
+// thread per row (fewer rows than fill the GPU with 256-row blocks).
+bool few_rows(int64_t T, const DeviceInfo* di) { return cdiv(T, 256) < di->sms; }
+
 }  // namespace
 
 // ============================================================================= C ABI
@@ -615,7 +619,9 @@ size_t lp_fwd_workspace_bytes(int64_t T, int64_t Vs) {
   if (T <= 0 || Vs <= 0) return 256;
   const int cg = cta_group_for(CG_FWD);
   GemmSched s = plan_fwd(T, Vs, 64, di != nullptr ? workers(di, cg) : (cg == 1 ? sms : sms / 2), 128 * cg);
-  return align_up((size_t)2 * s.n_groups * T * sizeof(float2), 256) + align_up((size_t)T * 4, 256);
+  // partials, target logits, and the [3, T] triples lp_fwd_sum merges first when T is small
+  return align_up((size_t)2 * s.n_groups * T * sizeof(float2), 256) + align_up((size_t)T * 4, 256) +
+         align_up((size_t)T * 12, 256);
 }
 
 int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
@@ -649,9 +655,14 @@ int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const
   set_hints(p, G_FWD);
   if ((rc = launch_gemm_cap<EPI_FWD_LSE, false, false>(softcap > 0.f, st, ta, tb, ta, p, di, "fwd_lse_gemm"))) return rc;
   ProfScope prof(st, "fwd_finalize");
-  fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, 2 * s.n_groups, (int)T, tgt, y, v_off, Vs, stats,
-                                                              logp);
-  LP_LAUNCH_CHECK("fwd_finalize_kernel");
+  if (few_rows(T, di)) {
+    fwd_finalize_rows_kernel<<<(unsigned)T, 128, 0, st>>>(part, 2 * s.n_groups, (int)T, tgt, y, v_off, Vs, stats, logp);
+    LP_LAUNCH_CHECK("fwd_finalize_rows_kernel");
+  } else {
+    fwd_finalize_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(part, 2 * s.n_groups, (int)T, tgt, y, v_off, Vs, stats,
+                                                                logp);
+    LP_LAUNCH_CHECK("fwd_finalize_kernel");
+  }
   return LP_OK;
 }
 
@@ -680,11 +691,13 @@ int lp_fwd_sum(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, c
   const int cg = cta_group_for(CG_FWD);
   GemmSched s = plan_fwd(T, Vs, d, workers(di, cg), 128 * cg);
   const size_t part_bytes = align_up((size_t)2 * s.n_groups * T * sizeof(float2), 256);
-  const size_t need = part_bytes + align_up((size_t)T * 4, 256);
+  const size_t tgt_bytes = align_up((size_t)T * 4, 256);
+  const size_t need = part_bytes + tgt_bytes + align_up((size_t)T * 12, 256);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(LP_EWORKSPACE, "lp_fwd_sum needs %zu workspace bytes, got %zu", need, workspace_bytes);
   float2* part = reinterpret_cast<float2*>(workspace);
   float* tgt = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + part_bytes);
+  float* pre = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + part_bytes + tgt_bytes);
 
   alignas(64) CUtensorMap ta, tb;
   if ((rc = map_bf16(&ta, H, d, T, ldh, BK, 128, "hidden"))) return rc;
@@ -702,11 +715,105 @@ int lp_fwd_sum(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, c
   // other ranks
   const unsigned grid = (unsigned)std::min<int64_t>(cdiv(T, 256), di->sms);
   ProfScope prof(st, "fwd_finalize_mesh");
+  const bool merge_first = few_rows(T, di);
+  if (merge_first) {
+    fwd_finalize_rows_kernel<<<(unsigned)T, 128, 0, st>>>(part, 2 * s.n_groups, (int)T, tgt, y, v_off, Vs, pre,
+                                                          nullptr);
+    LP_LAUNCH_CHECK("fwd_finalize_rows_kernel");
+  }
   fwd_finalize_mesh_kernel<<<grid, 256, 0, st>>>(
       part, 2 * s.n_groups, (int)T, tgt, y, v_off, Vs, reinterpret_cast<float4*>(exchange_multicast),
       reinterpret_cast<const float4*>(exchange), ld_exchange, counter_multicast, counter, arrivals,
-      epoch * (unsigned)world, rank, world, (unsigned long long)timeout_ms * 1000000ull, logp, norm);
+      epoch * (unsigned)world, rank, world, (unsigned long long)timeout_ms * 1000000ull, merge_first ? pre : nullptr,
+      logp, norm);
   LP_LAUNCH_CHECK("fwd_finalize_mesh_kernel");
+  return LP_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Sampler head plan: the forward's chunk-major order with one vocabulary tile per unit, so
+// a decode batch (one or two M tiles) still spreads over every SM.
+GemmSched plan_head(int64_t B, int64_t V, int64_t d, int bm) {
+  GemmSched s = plan_fwd(B, V, d, 0, bm);
+  s.n_group = 1;
+  s.n_groups = s.tiles_n;
+  s.num_units = s.tiles_m * s.n_groups;
+  return s;
+}
+
+size_t head_part_bytes(const GemmSched& s, int64_t B) { return align_up((size_t)2 * s.n_groups * B * sizeof(float2), 256); }
+
+}  // namespace
+
+extern "C" {
+
+size_t lp_head_workspace_bytes(int64_t B, int64_t V) {
+  if (B <= 0 || V <= 0) return 256;
+  const int cg = cta_group_for(CG_FWD);
+  return 2 * head_part_bytes(plan_head(B, V, 64, 128 * cg), B);
+}
+
+int lp_head(void* stream, const void* H, int64_t B, int64_t d, int64_t ldh, const void* W, int64_t V, float softcap,
+            float* logits, int64_t ld_logits, int flags, float* norm, int32_t* argmax, float* argmax_logp,
+            void* workspace, size_t workspace_bytes) {
+  if (B < 0 || d <= 0 || V <= 0) return fail(LP_EINVAL, "bad sizes B=%lld d=%lld V=%lld", (long long)B, (long long)d,
+                                              (long long)V);
+  if (B > (int64_t)1 << 30 || V > (int64_t)1 << 30) return fail(LP_EINVAL, "B or V above 2^30");
+  if (d % 8 != 0) return fail(LP_EINVAL, "hidden size d=%lld must be a multiple of 8", (long long)d);
+  if (ldh < d || ldh % 8 != 0) return fail(LP_EINVAL, "ldh=%lld must be >= d and a multiple of 8", (long long)ldh);
+  if (W == nullptr || (B > 0 && H == nullptr)) return fail(LP_EINVAL, "null hidden or embedding");
+  if (flags & ~LP_HEAD_LOGPROBS) return fail(LP_EINVAL, "unknown lp_head flags %d", flags);
+  if (logits != nullptr) {
+    if (ld_logits < V || ld_logits % 4 != 0) return fail(LP_EINVAL, "ld_logits must be >= V and a multiple of 4");
+    if ((reinterpret_cast<uintptr_t>(logits) & 15) != 0) return fail(LP_EINVAL, "logits must be 16-byte aligned");
+  } else if (flags & LP_HEAD_LOGPROBS) {
+    return fail(LP_EINVAL, "LP_HEAD_LOGPROBS needs a logits buffer");
+  }
+  if ((flags & LP_HEAD_LOGPROBS) && norm == nullptr) return fail(LP_EINVAL, "LP_HEAD_LOGPROBS needs norm");
+  if (B == 0) return LP_OK;
+  DeviceInfo* di = nullptr;
+  int rc = current_device_info(&di);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int cg = cta_group_for(CG_FWD);
+  GemmSched s = plan_head(B, V, d, 128 * cg);
+  const size_t pb = head_part_bytes(s, B);
+  if (workspace == nullptr || workspace_bytes < 2 * pb)
+    return fail(LP_EWORKSPACE, "lp_head needs %zu workspace bytes, got %zu", 2 * pb, workspace_bytes);
+  float2* part = reinterpret_cast<float2*>(workspace);
+  float2* best = reinterpret_cast<float2*>(reinterpret_cast<char*>(workspace) + pb);
+
+  alignas(64) CUtensorMap ta, tb, to;
+  if ((rc = map_bf16(&ta, H, d, B, ldh, BK, 128, "hidden"))) return rc;
+  if ((rc = map_bf16(&tb, W, d, V, d, BK, b_box_rows(cg), "embedding"))) return rc;
+  if (logits != nullptr) {
+    if ((rc = map_store_f32(&to, logits, V, B, ld_logits, "logits store"))) return rc;
+  } else {
+    to = ta;  // not used: no logits are stored
+  }
+  GemmParams p{};
+  p.s = s;
+  p.e.softcap = softcap;
+  p.e.part = part;
+  p.e.best = best;
+  p.e.store_logits = logits != nullptr ? 1 : 0;
+  set_hints(p, G_FWD);
+  if ((rc = launch_gemm_cap<EPI_HEAD, false, false>(softcap > 0.f, st, ta, tb, to, p, di, "head_gemm"))) return rc;
+  {
+    ProfScope prof(st, "head_finalize");
+    head_finalize_kernel<<<(unsigned)B, 256, 0, st>>>(part, best, 2 * s.n_groups, (int)B, norm, argmax, argmax_logp);
+    LP_LAUNCH_CHECK("head_finalize_kernel");
+  }
+  if (flags & LP_HEAD_LOGPROBS) {
+    ProfScope prof(st, "logits_to_logprobs");
+    const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(V / 4 + 1, 256), 64));
+    const unsigned gy = (unsigned)std::min<int64_t>(B, 65535);
+    logits_to_logprobs_kernel<<<dim3(gx, gy), 256, 0, st>>>(logits, ld_logits, (int)B, V, norm);
+    LP_LAUNCH_CHECK("logits_to_logprobs_kernel");
+  }
   return LP_OK;
 }
 

@@ -29,6 +29,9 @@
 //   EPI_BWD_DZ  : recompute path; dZ = g * (onehot - softmax) * softcap' written as bf16
 //                 through swizzled smem staging + TMA store.
 //   EPI_STORE   : plain f32 / bf16 store or f32 TMA reduce-add of the accumulator.
+//   EPI_HEAD    : sampler head: softcapped logits stored as f32 (optional), running
+//                 (max, sum-exp) per row in base 2 and the first column of the row maximum;
+//                 one partial of each per row per unit and column half.
 //
 // Synchronisation (all waits bounded, see lp_ptx.cuh):
 //   full[s]   : TMA -> MMA. CG=2: lives in the leader, counts both CTAs' bytes.
@@ -52,7 +55,7 @@ constexpr int STAGING_WARP_BYTES = 2 * STAGING_BUF_BYTES;  // double-buffered pe
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-enum : int { EPI_FWD_LSE = 0, EPI_BWD_DZ = 1, EPI_STORE = 2 };
+enum : int { EPI_FWD_LSE = 0, EPI_BWD_DZ = 1, EPI_STORE = 2, EPI_HEAD = 3 };
 enum : int { STORE_BF16 = 0, STORE_F32 = 1, STORE_F32_ADD = 2 };
 
 template <int CG>
@@ -87,6 +90,8 @@ struct EpiParams {
   float softcap;         // <= 0 means no softcap
   float2* part;          // FWD: [n_groups][M] (running max in base 2, running sum)
   float* tgt;            // FWD: [M] target logit (natural units), written by the owning tile
+  float2* best;          // HEAD: [n_groups][M] (largest logit, its column as int bits)
+  int store_logits;      // HEAD: store the logits through tmO (else only the row statistics)
   const float* g;        // DZ : [M] upstream d logp
   const float* stats;    // DZ : [2][stats_ld] global (max, sum) in natural units
   long long stats_ld;    // DZ : row stride of stats
@@ -544,6 +549,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // per-row state
       int yl = -1;
       float run_m = -INFINITY, run_s = 0.f;
+      float best_z = -INFINITY;  // HEAD: largest logit so far (natural units) and its column
+      int best_i = -1;
       float gv = 0.f, l2 = 0.f;
       if (EPI == EPI_FWD_LSE) {
         if (row_ok) {
@@ -685,6 +692,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             sb ^= 1;
           }
+        } else if constexpr (EPI == EPI_HEAD) {
+          // z = c * tanh(x / c) = c * (1 - 2 r), r = 1 / (1 + 2^(2x log2(e) / c)), or z = x
+#pragma unroll 1
+          for (int pc = 0; pc < BN / 32; ++pc) {
+            uint32_t r[16];
+            __syncwarp();
+            tmem_ld16(taddr + pc * 16, r);
+            tmem_wait_ld16(r);
+            const int col0 = colh + pc * 16;
+            const int nvalid = S.N - col0;  // columns >= nvalid are vocabulary padding (warp-uniform)
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float x = __uint_as_float(r[j]);
+              const float z = HAS_CAP ? fmaf(-2.f * cap, fast_rcp(1.f + fast_ex2(x * k1)), cap) : x;
+              r[j] = __float_as_uint(z);
+              if (j < nvalid) {
+                if (z > best_z) {  // strict: the first column of a tie is kept
+                  best_z = z;
+                  best_i = col0 + j;
+                }
+                mx = fmaxf(mx, z);
+              }
+            }
+            if (nvalid > 0) {
+              const float nm = fmaxf(run_m, mx * kLog2e);
+              const float scale = (nm == run_m) ? 1.f : fast_ex2(run_m - nm);
+              float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+              for (int j = 0; j < 16; j += 2) {
+                if (j < nvalid) s0 += fast_ex2(fmaf(__uint_as_float(r[j]), kLog2e, -nm));
+                if (j + 1 < nvalid) s1 += fast_ex2(fmaf(__uint_as_float(r[j + 1]), kLog2e, -nm));
+              }
+              run_s = fmaf(run_s, scale, s0 + s1);
+              run_m = nm;
+            }
+            if (E.store_logits && nvalid > 0) {
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
+              uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
+              const uint32_t sbase = smem_u32(buf_s);
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                st_shared_v4(sbase + sw64_offset(lane, c), r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmO, buf_s, col0, row_base);
+                bulk_commit();
+              }
+              sb ^= 1;
+            }
+          }
         } else {  // EPI_STORE
           const int row0 = un.split * E.split_rows + row_base;
           if (E.store_mode == STORE_BF16) {
@@ -798,9 +858,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
 
-      if constexpr (EPI == EPI_FWD_LSE) {
+      if constexpr (EPI == EPI_FWD_LSE || EPI == EPI_HEAD) {
         // one (max, sum) partial per unit and column half
         if (row_ok) E.part[(size_t)(un.group * 2 + h) * S.M + row] = make_float2(run_m, run_s);
+      }
+      if constexpr (EPI == EPI_HEAD) {
+        if (row_ok) E.best[(size_t)(un.group * 2 + h) * S.M + row] = make_float2(best_z, __int_as_float(best_i));
       }
     }
     if (EPI != EPI_FWD_LSE) {

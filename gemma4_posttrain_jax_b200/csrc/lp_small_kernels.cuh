@@ -33,6 +33,52 @@ __global__ void fwd_finalize_kernel(const float2* __restrict__ part, int n_group
   if (logp != nullptr) logp[t] = tgt - (mx + logf(s));
 }
 
+// fwd_finalize_kernel for few rows with many partials (small T: one block per row, each
+// thread folds a strided subset of the partials, then the block reduces). Same outputs.
+__global__ void fwd_finalize_rows_kernel(const float2* __restrict__ part, int n_groups, int T,
+                                         const float* __restrict__ tgt_ws, const int32_t* __restrict__ y,
+                                         long long v_off, long long Vs, float* __restrict__ stats,
+                                         float* __restrict__ logp) {
+  __shared__ float2 warp_ms[32];
+  const int t = blockIdx.x;
+  float m = -INFINITY, s = 0.f;
+  for (int g = threadIdx.x; g < n_groups; g += blockDim.x) {
+    const float2 p = part[(size_t)g * T + t];
+    if (p.x == -INFINITY) continue;
+    const float nm = fmaxf(m, p.x);
+    s = s * exp2f(m - nm) + p.y * exp2f(p.x - nm);
+    m = nm;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float om = __shfl_down_sync(0xffffffffu, m, off);
+    const float os = __shfl_down_sync(0xffffffffu, s, off);
+    const float nm = fmaxf(m, om);
+    if (nm != -INFINITY) {
+      s = (m == -INFINITY ? 0.f : s * exp2f(m - nm)) + (om == -INFINITY ? 0.f : os * exp2f(om - nm));
+      m = nm;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) warp_ms[threadIdx.x >> 5] = make_float2(m, s);
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+    const float2 o = warp_ms[w];
+    const float nm = fmaxf(m, o.x);
+    if (nm == -INFINITY) continue;
+    s = (m == -INFINITY ? 0.f : s * exp2f(m - nm)) + (o.x == -INFINITY ? 0.f : o.y * exp2f(o.x - nm));
+    m = nm;
+  }
+  const long long local = (long long)y[t] - v_off;
+  const bool owned = local >= 0 && local < Vs;
+  const float tgt = owned ? tgt_ws[t] : 0.f;
+  const float mx = m * kLn2;
+  stats[t] = mx;
+  stats[(size_t)T + t] = s;
+  stats[(size_t)2 * T + t] = tgt;
+  if (logp != nullptr) logp[t] = tgt - (mx + logf(s));
+}
+
 // Per-row (max, sum, owned target) of this shard from the forward GEMM's partials.
 __device__ __forceinline__ float3 shard_triple(const float2* __restrict__ part, int n_groups, int T, int t,
                                                const float* __restrict__ tgt_ws, const int32_t* __restrict__ y,
@@ -52,7 +98,8 @@ __device__ __forceinline__ float3 shard_triple(const float2* __restrict__ part, 
 // The forward's finalize on one rank of a vocabulary mesh, fused with the exchange of the
 // per-shard triples over NVLink (the pmax / psum of losses.py:219,243-245):
 //   1. every thread merges its rows' partials into this shard's (max, sum, owned target)
-//      and stores them, as one 16-byte multimem store, into slot `rank` of every rank's
+//      (or reads them from `pre`, merged by fwd_finalize_rows_kernel when T is small) and
+//      stores them, as one 16-byte multimem store, into slot `rank` of every rank's
 //      copy of the exchange buffer [world][ld] (f32x4);
 //   2. the last block of this launch to finish step 1 (an arrival counter in this GPU's
 //      memory) adds 1 to the exchange counter in every copy (release at system scope);
@@ -66,11 +113,14 @@ __global__ void fwd_finalize_mesh_kernel(const float2* __restrict__ part, int n_
                                          long long v_off, long long Vs, float4* xch_mc, const float4* xch_local,
                                          long long ld, unsigned* cnt_mc, const unsigned* cnt_local, unsigned* arrivals,
                                          unsigned target, int rank, int world, unsigned long long limit_ns,
-                                         float* __restrict__ logp, float* __restrict__ norm) {
+                                         const float* __restrict__ pre, float* __restrict__ logp,
+                                         float* __restrict__ norm) {
   __shared__ int s_go;
   const int stride = gridDim.x * blockDim.x;
   for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += stride) {
-    const float3 v = shard_triple(part, n_groups, T, t, tgt_ws, y, v_off, Vs);
+    // the triples were merged beforehand (pre, [3, T]) when there are few rows
+    const float3 v = pre != nullptr ? make_float3(pre[t], pre[(size_t)T + t], pre[(size_t)2 * T + t])
+                                    : shard_triple(part, n_groups, T, t, tgt_ws, y, v_off, Vs);
     multimem_st_f32x4(xch_mc + (size_t)rank * ld + t, make_float4(v.x, v.y, v.z, 0.f));
   }
   __syncthreads();
@@ -114,6 +164,83 @@ __global__ void fwd_finalize_mesh_kernel(const float2* __restrict__ part, int n_
       norm[t] = m;
       norm[(size_t)T + t] = s;
     }
+  }
+}
+
+// Sampler head: merge the per-unit partials of each row into the normaliser (max in
+// natural units, sum exp(z - max)), the first column of the row maximum and its logp. One
+// block per row (a decode batch has few rows and many partials): each thread folds a
+// strided subset of the partials, then the block reduces. Ties keep the smaller column
+// (the first occurrence, as argmax does).
+struct HeadAcc {
+  float m, s, bz;  // running max (base 2) and sum, best logit
+  int bi;          // its column (-1: none yet)
+};
+
+__device__ __forceinline__ HeadAcc head_merge(HeadAcc a, HeadAcc b) {
+  HeadAcc r;
+  r.m = fmaxf(a.m, b.m);
+  r.s = (a.m == -INFINITY ? 0.f : a.s * exp2f(a.m - r.m)) + (b.m == -INFINITY ? 0.f : b.s * exp2f(b.m - r.m));
+  const bool take_b = b.bi >= 0 && (a.bi < 0 || b.bz > a.bz || (b.bz == a.bz && b.bi < a.bi));
+  r.bz = take_b ? b.bz : a.bz;
+  r.bi = take_b ? b.bi : a.bi;
+  return r;
+}
+
+__global__ void head_finalize_kernel(const float2* __restrict__ part, const float2* __restrict__ best, int n_parts,
+                                     int B, float* __restrict__ norm, int32_t* __restrict__ argmax,
+                                     float* __restrict__ argmax_logp) {
+  __shared__ HeadAcc warp_acc[32];
+  const int t = blockIdx.x;
+  HeadAcc acc{-INFINITY, 0.f, -INFINITY, -1};
+  for (int g = threadIdx.x; g < n_parts; g += blockDim.x) {
+    const float2 p = part[(size_t)g * B + t];
+    const float2 b = best[(size_t)g * B + t];
+    acc = head_merge(acc, HeadAcc{p.x, p.y, b.x, __float_as_int(b.y)});
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    HeadAcc o;
+    o.m = __shfl_down_sync(0xffffffffu, acc.m, off);
+    o.s = __shfl_down_sync(0xffffffffu, acc.s, off);
+    o.bz = __shfl_down_sync(0xffffffffu, acc.bz, off);
+    o.bi = __shfl_down_sync(0xffffffffu, acc.bi, off);
+    acc = head_merge(acc, o);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) warp_acc[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) acc = head_merge(acc, warp_acc[w]);
+    const float mx = acc.m * kLn2;
+    if (norm != nullptr) {
+      norm[t] = mx;
+      norm[(size_t)B + t] = acc.s;
+    }
+    if (argmax != nullptr) argmax[t] = acc.bi;
+    if (argmax_logp != nullptr) argmax_logp[t] = acc.bz - (mx + logf(acc.s));
+  }
+}
+
+// logits[b, v] -= max_b + log(sum_b) in place: the full log-softmax of the sampler. Rows are
+// 16-byte aligned (ld % 4 == 0, the TMA store's requirement); blockIdx.y strides the rows.
+__global__ void logits_to_logprobs_kernel(float* __restrict__ logits, long long ld, int B, long long V,
+                                          const float* __restrict__ norm) {
+  const long long v4 = V / 4;
+  for (int b = blockIdx.y; b < B; b += gridDim.y) {
+    const float lse = norm[b] + logf(norm[(size_t)B + b]);
+    float* row = logits + (size_t)b * ld;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < v4; i += (long long)gridDim.x * blockDim.x) {
+      float4 x = reinterpret_cast<float4*>(row)[i];
+      x.x -= lse;
+      x.y -= lse;
+      x.z -= lse;
+      x.w -= lse;
+      reinterpret_cast<float4*>(row)[i] = x;
+    }
+    for (long long v = 4 * v4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; v < V;
+         v += (long long)gridDim.x * blockDim.x)
+      row[v] -= lse;
   }
 }
 

@@ -138,6 +138,44 @@ def shard_forward_sum(
     return logp, norm
 
 
+def head(
+    embed: torch.Tensor,
+    hidden: torch.Tensor,
+    softcap: float | None,
+    *,
+    want_logits: bool = True,
+    log_probs: bool = False,
+) -> tuple[torch.Tensor | None, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """``lp_head`` over the whole vocabulary for B rows: (logits f32 [B, V] or None,
+    normalization [2, B], argmax int32 [B], logp of the argmax [B]). ``log_probs`` makes the
+    first output the full log-softmax instead of the logits."""
+    dev = _require_cuda(embed, hidden)
+    _check_bf16("embedding", embed)
+    _check_bf16("hidden", hidden)
+    if log_probs and not want_logits:
+        raise ValueError("log_probs needs want_logits")
+    lib = _lib.load()
+    h2, ldh = _rows(hidden)
+    B, d = h2.shape
+    V = embed.shape[0]
+    w = embed if embed.is_contiguous() else embed.contiguous()
+    ld = -(-V // 4) * 4
+    logits = torch.empty((B, ld), dtype=torch.float32, device=dev)[:, :V] if want_logits else None
+    norm = torch.empty((2, B), dtype=torch.float32, device=dev)
+    top = torch.empty((B,), dtype=torch.int32, device=dev)
+    top_logp = torch.empty((B,), dtype=torch.float32, device=dev)
+    if B == 0:
+        return logits, norm, top, top_logp
+    ws, wsp, wsn = _workspace(lib.lp_head_workspace_bytes(B, V), dev)
+    cap = float(softcap) if softcap is not None else 0.0
+    rc = lib.lp_head(
+        _stream(dev), _ptr(h2), B, d, ldh, _ptr(w), V, cap, _ptr(logits), ld,
+        _lib.LP_HEAD_LOGPROBS if log_probs else 0, _ptr(norm), _ptr(top), _ptr(top_logp), wsp, wsn,
+    )
+    _lib.check(rc, "lp_head")
+    return logits, norm, top, top_logp
+
+
 def combine(shard_stats: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """``lp_combine``: [P, 3, T] per-shard triples -> (logp [T], normalization [2, T])."""
     dev = _require_cuda(shard_stats)

@@ -219,6 +219,30 @@ LP_API int lp_bwd_sum(void* stream, const void* H, int64_t T, int64_t d, int64_t
                       int world, int timeout_ms, void* dW, int flags, int64_t token_chunk, void* workspace,
                       size_t workspace_bytes);
 
+/* lp_head flags */
+#define LP_HEAD_LOGPROBS 1 /* the logits buffer receives log-probabilities z - logsumexp(z) */
+
+/* Scratch bytes lp_head needs for B rows against V vocabulary rows. */
+LP_API size_t lp_head_workspace_bytes(int64_t B, int64_t V);
+
+/*
+ * Sampler LM head (replaces forward_lm_head, model.py:676-680, and the full-vocabulary
+ * log-softmax and greedy pick of _sample_token, sampler.py:145-161,184): one tensor-core
+ * GEMM over the whole vocabulary for B decode rows, with the softcap, a running
+ * log-sum-exp and the row argmax in its epilogue.
+ *   H        bf16 [B, ldh]                W  bf16 [V, d] (the whole vocabulary)
+ *   logits   f32 [B, ld_logits] (ld_logits >= V, % 4 == 0, 16-byte aligned) or NULL: the
+ *            softcapped logits z, or with LP_HEAD_LOGPROBS the log-probabilities
+ *            z - (max + log sum); NULL skips the [B, V] store (greedy decoding needs none)
+ *   norm     f32 [2, B] or NULL: row max of z and sum exp(z - max) (needed with LOGPROBS)
+ *   argmax   int32 [B] or NULL: first column of the row maximum (greedy token)
+ *   argmax_logp  f32 [B] or NULL: log-probability of that column
+ * The workspace is lp_head_workspace_bytes(B, V).
+ */
+LP_API int lp_head(void* stream, const void* H, int64_t B, int64_t d, int64_t ldh, const void* W, int64_t V,
+                   float softcap, float* logits, int64_t ld_logits, int flags, float* norm, int32_t* argmax,
+                   float* argmax_logp, void* workspace, size_t workspace_bytes);
+
 /* Scratch bytes lp_compact needs for B * N response slots. */
 LP_API size_t lp_compact_workspace_bytes(int64_t B, int64_t N);
 

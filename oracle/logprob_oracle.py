@@ -356,3 +356,43 @@ def compact_response(completion_mask: np.ndarray):
     """
     flat = np.asarray(completion_mask).reshape(-1).astype(bool)
     return np.nonzero(flat)[0].astype(np.int64)
+
+
+def lm_head(embed: np.ndarray, hidden: np.ndarray, softcap: float | None):
+    """Sampler head: ``forward_lm_head`` (``model.py:676-680``) then the full log-softmax and
+    greedy pick of ``_sample_token`` (``sampler.py:150-161,184``), in float64.
+
+    Returns (logits [B, V], full_logps [B, V], (max, sum exp(z - max)) [2, B], argmax [B]
+    (first column of the row maximum, as ``jnp.argmax``), logp of the argmax [B]).
+    """
+    h = hidden.reshape(-1, hidden.shape[-1]).astype(np.float64)
+    logits = h @ embed.astype(np.float64).T
+    if softcap is not None:
+        logits = np.tanh(logits / softcap) * softcap
+    m = logits.max(axis=-1)
+    s = np.exp(logits - m[:, None]).sum(axis=-1)
+    full = logits - (m + np.log(s))[:, None]
+    top = logits.argmax(axis=-1)
+    return logits, full, np.stack((m, s)), top, full[np.arange(top.size), top]
+
+
+def top_k_top_p_keep(scores: np.ndarray, top_k: int, top_p: float) -> np.ndarray:
+    """Boolean [B, V] of the columns ``_sample_token`` may sample (``sampler.py:162-181``):
+    the ``top_k`` largest scores (0 or >= V: all), then within them (or within all columns,
+    sorted descending, stable) the shortest prefix whose probability reaches ``top_p``; the
+    most likely column is always kept."""
+    B, V = scores.shape
+    order = np.argsort(-scores, axis=-1, kind="stable")
+    if 0 < top_k < V:
+        order = order[:, :top_k]
+    keep = np.zeros((B, V), dtype=bool)
+    for b in range(B):
+        cols = order[b]
+        if top_p < 1:
+            sc = scores[b, cols].astype(np.float64)
+            w = np.exp(sc - sc.max())
+            p = w / w.sum()
+            prev = np.concatenate(([0.0], np.cumsum(p)[:-1]))
+            cols = cols[(prev < top_p) | (np.arange(cols.size) == 0)]
+        keep[b, cols] = True
+    return keep

@@ -88,6 +88,20 @@ def test_small_entry_points_validate(lib):
     _einval(lib.lp_compact(None, None, 2, 3, None, 0, 0, 0, 0, None, None, None, fake, fake, fake, fake, 1024), lib,
             "null mask")
     _einval(lib.lp_gemm_bf16(None, fake, 0, 8, 8, 0, fake, 8, 8, 0, fake, 8), lib, "sizes")
+    # sampler head: logits row stride and flag checks run before any device work
+    _einval(lib.lp_head(None, fake, 4, 8, 8, fake, 10, 0.0, fake, 9, 0, fake, fake, fake, fake, 1024), lib,
+            "ld_logits")
+    _einval(lib.lp_head(None, fake, 4, 8, 8, fake, 10, 0.0, None, 12, 1, fake, fake, fake, fake, 1024), lib,
+            "LP_HEAD_LOGPROBS")
+    _einval(lib.lp_head(None, fake, 4, 8, 8, fake, 10, 0.0, fake, 12, 4, fake, fake, fake, fake, 1024), lib,
+            "flags")
+    # mesh forward: rank / epoch / exchange checks
+    _einval(lib.lp_fwd_sum(None, fake, 4, 8, 8, fake, 10, 0, fake, 0.0, fake, fake, 4, fake, fake, fake, 1, 2, 2,
+                           100, fake, fake, fake, 1 << 20), lib, "rank")
+    _einval(lib.lp_fwd_sum(None, fake, 4, 8, 8, fake, 10, 0, fake, 0.0, fake, fake, 4, fake, fake, fake, 0, 0, 2,
+                           100, fake, fake, fake, 1 << 20), lib, "epoch")
+    _einval(lib.lp_fwd_sum(None, fake, 4, 8, 8, fake, 10, 0, fake, 0.0, fake, fake, 2, fake, fake, fake, 1, 0, 2,
+                           100, fake, fake, fake, 1 << 20), lib, "ld_exchange")
 
 
 def test_loader_fails_loudly_when_library_missing(tmp_path):

@@ -127,3 +127,28 @@ def test_bf16_round_ties_to_even():
 def test_compaction_order():
     m = np.array([[1, 0, 1], [0, 0, 0], [1, 1, 0]], bool)
     np.testing.assert_array_equal(orc.compact_response(m), [0, 2, 6, 7])
+
+
+@pytest.mark.parametrize("softcap", [None, 3.0])
+def test_sampler_head_oracle_consistent_with_dense(softcap):
+    rng = np.random.default_rng(17)
+    w = orc.bf16_round(rng.normal(size=(23, 7)) * 0.7)
+    h = orc.bf16_round(rng.normal(size=(5, 7)))
+    z, full, norm, top, top_logp = orc.lm_head(w, h, softcap)
+    y = rng.integers(0, 23, size=5)
+    np.testing.assert_allclose(full[np.arange(5), y], orc.dense_logps(w, h, y, softcap), atol=1e-12)
+    np.testing.assert_allclose(norm, orc.dense_normalization(w, h, softcap), rtol=1e-12)
+    np.testing.assert_allclose(np.exp(full).sum(-1), 1.0, atol=1e-12)
+    assert (z[np.arange(5), top] == z.max(-1)).all()
+    np.testing.assert_allclose(top_logp, full.max(-1), atol=1e-12)
+
+
+def test_top_k_top_p_keep_semantics():
+    scores = np.log(np.array([[0.5, 0.1, 0.3, 0.1], [0.25, 0.25, 0.25, 0.25]]))
+    keep = orc.top_k_top_p_keep(scores, 2, 1.0)
+    assert keep.tolist() == [[True, False, True, False], [True, True, False, False]]
+    # top_p 0.6 keeps the shortest descending prefix reaching 0.6 (0.5 < 0.6, 0.5+0.3 >= 0.6)
+    keep = orc.top_k_top_p_keep(scores, 0, 0.6)
+    assert keep.tolist() == [[True, False, True, False], [True, True, True, False]]
+    # the most likely column is always kept
+    assert orc.top_k_top_p_keep(scores, 0, 1e-9).sum(-1).tolist() == [1, 1]
