@@ -144,7 +144,15 @@ struct DeviceInfo {
 };
 
 // Persistent workers of a launch: SMs for CG = 1, co-resident CTA pairs for CG = 2.
-int workers(const DeviceInfo* di, int cg) { return cg == 1 ? di->sms : di->pairs; }
+// LP_B200_MAX_CTAS caps the CTAs of a GEMM launch (a tuning aid: fewer SMs share L2 / HBM).
+int workers(const DeviceInfo* di, int cg) {
+  static const int cap = [] {
+    const char* e = getenv("LP_B200_MAX_CTAS");
+    return (e != nullptr && atoi(e) > 0) ? atoi(e) : 0;
+  }();
+  const int w = cg == 1 ? di->sms : di->pairs;
+  return cap > 0 ? std::max(1, std::min(w, cap / cg)) : w;
+}
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
 

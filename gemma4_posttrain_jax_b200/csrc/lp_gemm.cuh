@@ -42,6 +42,18 @@
 
 #include "lp_ptx.cuh"
 
+// Shared-memory ring depth per CTA group: the largest that fits 227 KB with the epilogue
+// staging (single CTAs: 4 x 48 KB, pairs: 6 x 32 KB). Measured (pipeline counters, config-2
+// workload): the single-CTA forward waits 639 / 207 / 103 cycles per K block for its loads
+// with 2 / 3 / 4 stages; the pairs gain nothing from a 6th stage over 5. Overridable at
+// build time for tuning.
+#ifndef LP_STAGES_CG1
+#define LP_STAGES_CG1 4
+#endif
+#ifndef LP_STAGES_CG2
+#define LP_STAGES_CG2 6
+#endif
+
 namespace lpk {
 
 constexpr int BN = 256;
@@ -64,7 +76,7 @@ struct Cfg {
   static constexpr int B_ROWS = BN / CG;                   // rows of B staged by each CTA
   static constexpr int B_STAGE_BYTES = B_ROWS * BK * 2;    // 32 KB (CG=1) / 16 KB (CG=2)
   static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
-  static constexpr int NUM_STAGES = CG == 1 ? 4 : 6;
+  static constexpr int NUM_STAGES = CG == 1 ? LP_STAGES_CG1 : LP_STAGES_CG2;
 };
 
 struct GemmSched {
