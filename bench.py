@@ -13,7 +13,8 @@ per-token (max, sum, target) triples are all-gathered and merged, dH partials al
 A step = one call of the public API (``completion_logps``) + its backward on that batch:
 compaction, fused LM-head GEMM + online LSE, combine, recompute backward into dZ, dH and dW
 tensor-core GEMMs, scatter back. ``value`` has the inputs resident in HBM; ``e2e`` adds the
-host->device copy of the step's inputs (pinned) and the device->host read of the logps.
+host->device copy of every step's inputs (pinned; double-buffered, so step k+1's copy runs
+on the copy engines while step k computes) and the device->host read of the logps.
 
 ``--impl reference`` times the CPU restatement of the reference's native path
 (``oracle/``; the reference itself is JAX-only and JAX is not installable here) on this
@@ -45,10 +46,10 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) per launch of each GEMM on this workload at N=1, from one ncu
 # capture (profiles/dram_traffic_grpo_config2_1gpu.md); backward launches: an 8192-row chunk.
 NCU_TRAFFIC_PER_LAUNCH_N1 = {
-    "fwd_lse_gemm": 22.70e9,
-    "bwd_dz_gemm": 5.73e9,
-    "bwd_dh_gemm": 20.40e9,
-    "bwd_dw_gemm": 11.58e9,
+    "fwd_lse_gemm": 20.01e9,
+    "bwd_dz_gemm": 6.00e9,
+    "bwd_dh_gemm": 10.81e9,
+    "bwd_dw_gemm": 7.83e9,
 }
 
 
@@ -465,28 +466,47 @@ def main():
     # ---------------------------------------------------------------- end-to-end (host buffers)
     e2e = None
     if not args.no_e2e:
+        # Every step copies its inputs from pinned host memory and reads its logps back. The
+        # inputs are double-buffered: step k+1's host->device copies run on a copy stream
+        # (copy engines) while step k computes, as a data loader would feed the trainer.
         hosts = [x.detach().cpu().pin_memory() for x in inputs]
-        devs = [torch.empty_like(x) for x in inputs]
+        bufs = [[torch.empty_like(x) for x in inputs] for _ in range(2)]
         out_shape = (args.batch, RESP) if args.config == 2 else (n_valid,)
         out_host = torch.empty(out_shape, dtype=torch.float32).pin_memory()
         h2d = sum(x.nbytes for x in hosts)
         d2h = out_host.nbytes
+        copy_stream = torch.cuda.Stream(dev)
+        compute_done = [torch.cuda.Event() for _ in range(2)]
+        copied = [torch.cuda.Event() for _ in range(2)]
+        for ev in compute_done:
+            ev.record()
 
-        def e2e_step():
-            for hx, dx in zip(hosts, devs):
-                dx.copy_(hx, non_blocking=True)
-            out = step(*devs)
-            out_host.copy_(out[0].detach(), non_blocking=True)
+        def issue_copy(k):
+            b = k % 2
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(compute_done[b])  # step k-2 no longer reads buffer b
+                for hx, dx in zip(hosts, bufs[b]):
+                    dx.copy_(hx, non_blocking=True)
+                copied[b].record(copy_stream)
 
-        for _ in range(args.warmup):
-            e2e_step()
+        def e2e_run(nsteps):
+            issue_copy(0)
+            for k in range(nsteps):
+                b = k % 2
+                if k + 1 < nsteps:
+                    issue_copy(k + 1)
+                torch.cuda.current_stream().wait_event(copied[b])
+                out = step(*bufs[b])
+                compute_done[b].record()
+                out_host.copy_(out[0].detach(), non_blocking=True)
+
+        e2e_run(args.warmup)
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
-            e2e_step()
+        e2e_run(args.steps)
         e1.record()
         torch.cuda.synchronize()
         barrier()
