@@ -473,12 +473,13 @@ int launch_gemm_cap(bool cap, cudaStream_t st, const CUtensorMap& a, const CUten
 // 1 evict_first, 2 evict_last). Measured (ncu DRAM bytes per launch at the config-2 size):
 // plain loads keep the forward and the dZ recompute near their algorithmic traffic;
 // evict_first on an operand that concurrent CTAs share (W) multiplies HBM reads, and an
-// explicit evict_normal policy is not the same as no hint. The dW GEMM keeps its H chunk
-// (re-read by every vocabulary tile) with evict_last. LP_B200_L2HINTS="fA fB zA zB hA hB wA wB" (8 digits: forward,
-// dZ recompute, dH, dW) overrides them for tuning.
+// explicit evict_normal policy is not the same as no hint. With the dynamic scheduler the
+// dW GEMM is also faster with plain loads than with evict_last on its H chunk (715 vs 734
+// cycles per K block, pipeline counters). LP_B200_L2HINTS="fA fB zA zB hA hB wA wB"
+// (8 digits: forward, dZ recompute, dH, dW) overrides them for tuning.
 enum GemmKind { G_FWD = 0, G_DZ = 1, G_DH = 2, G_DW = 3 };
 int l2_hint(GemmKind k, int operand) {
-  static int table[8] = {0, 0, 0, 0, 0, 0, 0, 2};
+  static int table[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   static std::once_flag once;
   std::call_once(once, [] {
     const char* e = getenv("LP_B200_L2HINTS");
