@@ -91,3 +91,21 @@ def test_dh_reduce_mode_single_shard_and_override(monkeypatch):
     assert sharding.peer_timeout_ms() == 250
     monkeypatch.setenv("LP_B200_PEER_TIMEOUT_MS", "0")
     assert sharding.peer_timeout_ms() == 1
+
+
+def test_stats_exchange_alternates_buffers_and_counts_epochs():
+    """lp_fwd_sum's bookkeeping: calls alternate between the two exchange buffers (so a rank
+    never overwrites a slot a peer may still read), and call k of a buffer waits for k * world
+    on a counter that is never reset."""
+    from gemma4_posttrain_jax_b200.sharding import StatsExchange
+
+    x = object.__new__(StatsExchange)  # the bookkeeping only; no symmetric memory on CPU
+    x.slot_bytes, x.base, x.base_mc, x.calls = 1 << 20, 0x10000000, 0x70000000, 0
+    calls = [x.next_call() for _ in range(5)]
+    xch = [c[0] for c in calls]
+    assert xch == [x.base, x.base + x.slot_bytes] * 2 + [x.base]
+    assert [c[1] - c[0] for c in calls] == [x.base_mc - x.base] * 5  # multicast twin of each buffer
+    assert [c[5] for c in calls] == [1, 1, 2, 2, 3]  # epoch per buffer
+    counters = {c[2] for c in calls}
+    assert len(counters) == 2 and all(c >= x.base + 2 * x.slot_bytes for c in counters)
+    assert len({c[4] for c in calls}) == 1  # one local arrival counter
