@@ -107,3 +107,20 @@ def test_small_entry_points_validate(lib):
 def test_loader_fails_loudly_when_library_missing(tmp_path):
     with pytest.raises(_lib.LogprobLibraryError, match="no CPU fallback"):
         _lib.load(tmp_path / "liblp_b200.so")
+
+
+def test_plain_c_caller_links_and_gets_error_codes(lib, tmp_path):
+    """A C program compiled against include/lp_logprob.h and linked to the library (what a
+    cgo / JNI binding does) gets sizes and LP_EINVAL codes with messages, without a GPU."""
+    src = Path(__file__).resolve().parent / "c_abi" / "abi_smoke.c"
+    exe = tmp_path / "abi_smoke"
+    libdir = _lib.LIB_PATH.parent
+    cc = subprocess.run(
+        ["gcc", "-std=c11", "-Wall", "-Werror", f"-I{HEADER.parent}", str(src), f"-L{libdir}", "-llp_b200",
+         f"-Wl,-rpath,{libdir}", "-o", str(exe)],
+        capture_output=True, text=True,
+    )
+    assert cc.returncode == 0, cc.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert "c abi smoke: ok" in run.stdout
