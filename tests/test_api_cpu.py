@@ -109,3 +109,47 @@ def test_stats_exchange_alternates_buffers_and_counts_epochs():
     counters = {c[2] for c in calls}
     assert len(counters) == 2 and all(c >= x.base + 2 * x.slot_bytes for c in counters)
     assert len({c[4] for c in calls}) == 1  # one local arrival counter
+
+
+def test_mesh_forward_routes_to_the_nvlink_exchange_or_the_all_gather(monkeypatch):
+    """With a multicast exchange buffer the forward of a vocabulary mesh is one lp_fwd_sum
+    call; without one it is lp_fwd + all-gather + lp_combine (the fallback never computes on
+    the host: the device calls are stubbed here and only the routing is checked)."""
+    import torch
+
+    from gemma4_posttrain_jax_b200 import losses
+
+    calls = []
+    H, y = torch.zeros(5, 8), torch.zeros(5, dtype=torch.int32)
+    W = torch.zeros(6, 8)
+    mesh = object()
+    logp, norm = torch.full((5,), -1.0), torch.ones(2, 5)
+
+    def fwd_sum(embed, hidden, targets, softcap, xch, *, vocab_offset, timeout_ms):
+        calls.append(("lp_fwd_sum", xch, vocab_offset, timeout_ms))
+        return logp, norm
+
+    def shard_forward(embed, hidden, targets, softcap, *, vocab_offset=0, want_logp=True):
+        calls.append(("lp_fwd", vocab_offset, want_logp))
+        return torch.zeros(3, 5), None
+
+    def gather(stats, m):
+        calls.append(("all_gather", m))
+        return torch.stack([stats, stats])
+
+    def combine(gathered):
+        calls.append(("lp_combine", tuple(gathered.shape)))
+        return logp, norm
+
+    monkeypatch.setattr(losses.ops, "shard_forward_sum", fwd_sum)
+    monkeypatch.setattr(losses.ops, "shard_forward", shard_forward)
+    monkeypatch.setattr(losses.ops, "combine", combine)
+    monkeypatch.setattr(losses, "all_gather_stats", gather)
+    monkeypatch.setenv("LP_B200_PEER_TIMEOUT_MS", "1234")
+    monkeypatch.setattr(losses, "stats_exchange", lambda m, rows, dev: "xch")
+    assert losses._mesh_forward(W, H, y, 30.0, mesh, 6) == (logp, norm)
+    assert calls == [("lp_fwd_sum", "xch", 6, 1234)]
+    calls.clear()
+    monkeypatch.setattr(losses, "stats_exchange", lambda m, rows, dev: None)
+    assert losses._mesh_forward(W, H, y, 30.0, mesh, 6) == (logp, norm)
+    assert calls == [("lp_fwd", 6, False), ("all_gather", mesh), ("lp_combine", (2, 3, 5))]
