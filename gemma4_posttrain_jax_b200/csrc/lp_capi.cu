@@ -244,6 +244,38 @@ int map_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, u
   return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, outer, ld_elems * 2, bi, bo, what);
 }
 
+// MN-major bf16 operand [k_extent rows][mn_extent columns] (row stride ld_elems) as a 3-D
+// map: dims (64 columns, K rows, mn_extent / 64 column chunks), box (64, 64, chunks), 128-byte
+// swizzle. One box lands in shared memory as `chunks` consecutive 8 KB [64 K rows x 128 B]
+// blocks, the layout of `chunks` 2-D 64x64 boxes side by side. Only for mn_extent % 64 == 0,
+// so the box never reaches past the tensor.
+int map_mn3d(CUtensorMap* m, const void* base, uint64_t mn_extent, uint64_t k_extent, uint64_t ld_elems,
+             uint32_t chunks, const char* what) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(LP_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  if (mn_extent % 64 != 0 || k_extent == 0) return fail(LP_EINVAL, "%s: 3-D map needs 64-column chunks", what);
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return fail(LP_EINVAL, "%s: base pointer not 16-byte aligned", what);
+  if ((ld_elems * 2) % 16 != 0 || ld_elems < mn_extent) return fail(LP_EINVAL, "%s: bad row stride", what);
+  cuuint64_t dims[3] = {64, k_extent, mn_extent / 64};
+  cuuint64_t strides[2] = {ld_elems * 2, 128};
+  cuuint32_t box[3] = {64, 64, chunks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LP_ECUDA, "%s: cuTensorMapEncodeTiled (3-D) failed (%d)", what, (int)r);
+  return LP_OK;
+}
+
+// 3-D MN-major operand maps (LP_B200_MN3D=0 keeps the per-chunk 2-D boxes, for tuning).
+bool mn3d_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("LP_B200_MN3D");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
 // Epilogue store targets: one 32-row x 64-byte box per warp and piece, 64-byte swizzle
 // (32 bf16 or 16 f32 columns), matching the staging layout of the GEMM epilogue.
 int map_store_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
@@ -924,8 +956,11 @@ int bwd_impl(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, con
     if (want_dh) {
       alignas(64) CUtensorMap ta, tb, to;
       if ((rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, BK, 128, "dZ as A"))) return rc;
-      if ((rc = map_bf16(&tb, W, d, Vs, d, 64, 64, "embedding as MN-major B"))) return rc;
       GemmParams p{};
+      p.b_mn3d = mn3d_enabled() && d % 64 == 0;
+      if (p.b_mn3d) rc = map_mn3d(&tb, W, d, Vs, d, b_box_rows(cg_dh) / 64, "embedding as MN-major B");
+      else rc = map_bf16(&tb, W, d, Vs, d, 64, 64, "embedding as MN-major B");
+      if (rc) return rc;
       const int wk = workers(di, cg_dh);
       p.s = plan_gemm(tcur, d, Vs, wk, ms == nullptr, 1, 128 * cg_dh);
       char* dh_c = reinterpret_cast<char*>(dH) + (size_t)t0 * ld_dh * (dh_f32 ? 4 : 2);
@@ -972,9 +1007,15 @@ int bwd_impl(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, con
     // 3) dW (+)= dZ^T . H_chunk
     if (want_dw) {
       alignas(64) CUtensorMap ta, tb, to;
-      if ((rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, 64, 64, "dZ as MN-major A"))) return rc;
-      if ((rc = map_bf16(&tb, Hc, d, tcur, ldh, 64, 64, "hidden as MN-major B"))) return rc;
       GemmParams p{};
+      p.a_mn3d = mn3d_enabled() && Vs % 64 == 0;
+      p.b_mn3d = mn3d_enabled() && d % 64 == 0;
+      if (p.a_mn3d) rc = map_mn3d(&ta, dz, Vs, tcur, L.ldz, 2, "dZ as MN-major A");
+      else rc = map_bf16(&ta, dz, Vs, tcur, L.ldz, 64, 64, "dZ as MN-major A");
+      if (rc) return rc;
+      if (p.b_mn3d) rc = map_mn3d(&tb, Hc, d, tcur, ldh, b_box_rows(cg_dw) / 64, "hidden as MN-major B");
+      else rc = map_bf16(&tb, Hc, d, tcur, ldh, 64, 64, "hidden as MN-major B");
+      if (rc) return rc;
       p.s = plan_gemm(Vs, d, tcur, workers(di, cg_dw), false, 1, 128 * cg_dw);
       const bool direct_bf16 = dw_bf16 && L.chunks == 1;
       if (direct_bf16) {

@@ -135,6 +135,9 @@ struct GemmParams {
   // Dynamic work distribution: units are claimed in order with atomicAdd on this counter
   // (zero at launch), so the units in flight always form a compact window of the unit order.
   unsigned int* sched;
+  // MN-major operands with 3-D tensor maps (64 columns, K, 64-column chunks): the CTA's
+  // tile of that operand is one TMA instruction instead of one per 64-column chunk.
+  int a_mn3d, b_mn3d;
 };
 
 __device__ __forceinline__ unsigned long long clk64() { return (unsigned long long)clock64(); }
@@ -370,12 +373,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
               if (!A_MN) {
                 ld1(a, &tmA, &full_bar[s], k0, a_row, hint_a, pol_a);
+              } else if (P.a_mn3d) {
+                tma_load_3d(a, &tmA, &full_bar[s], 0, k0, a_row / 64);
               } else {
                 ld1(a, &tmA, &full_bar[s], a_row, k0, hint_a, pol_a);
                 ld1(a + 8192, &tmA, &full_bar[s], a_row + 64, k0, hint_a, pol_a);
               }
               if (!B_MN) {
                 ld1(b, &tmB, &full_bar[s], k0, b_row, hint_b, pol_b);
+              } else if (P.b_mn3d) {
+                tma_load_3d(b, &tmB, &full_bar[s], 0, k0, b_row / 64);
               } else {
 #pragma unroll
                 for (int j = 0; j < C::B_ROWS / 64; ++j)
@@ -387,12 +394,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               const uint32_t fb = mapa_shared(smem_u32(&full_bar[s]), 0);
               if (!A_MN) {
                 ld2(a, &tmA, fb, k0, a_row, hint_a, pol_a);
+              } else if (P.a_mn3d) {
+                tma_load_3d_pair(a, &tmA, fb, 0, k0, a_row / 64);
               } else {
                 ld2(a, &tmA, fb, a_row, k0, hint_a, pol_a);
                 ld2(a + 8192, &tmA, fb, a_row + 64, k0, hint_a, pol_a);
               }
               if (!B_MN) {
                 ld2(b, &tmB, fb, k0, b_row, hint_b, pol_b);
+              } else if (P.b_mn3d) {
+                tma_load_3d_pair(b, &tmB, fb, 0, k0, b_row / 64);
               } else {
 #pragma unroll
                 for (int j = 0; j < C::B_ROWS / 64; ++j) ld2(b + 8192 * j, &tmB, fb, b_row + 64 * j, k0, hint_b, pol_b);
