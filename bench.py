@@ -47,9 +47,9 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # capture (profiles/dram_traffic_grpo_config2_1gpu.md); backward launches: an 8192-row chunk.
 NCU_TRAFFIC_PER_LAUNCH_N1 = {
     "fwd_lse_gemm": 20.01e9,
-    "bwd_dz_gemm": 6.00e9,
-    "bwd_dh_gemm": 10.81e9,
-    "bwd_dw_gemm": 7.83e9,
+    "bwd_dz_gemm": 5.98e9,
+    "bwd_dh_gemm": 10.92e9,
+    "bwd_dw_gemm": 8.37e9,
 }
 
 

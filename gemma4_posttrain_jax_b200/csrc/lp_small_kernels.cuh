@@ -268,16 +268,8 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int S, long
                                      void* __restrict__ out, long long ld_out, int out_bf16) {
   const long long n4 = N / 4;
   const long long total = M * n4;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / n4, c = (i % n4) * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < S; ++s) {
-      const float4 v = *reinterpret_cast<const float4*>(part + ((size_t)s * Mpad + r) * N + c);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
-    }
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  auto store = [&](long long r, long long c, const float4& acc) {
     if (out_bf16) {
       uint2 pk;
       pk.x = pack_bf16x2(acc.x, acc.y);
@@ -286,6 +278,30 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int S, long
     } else {
       *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + r * ld_out + c) = acc;
     }
+  };
+  // Two output vectors per thread and the split loop unrolled, so several independent
+  // 16-byte loads are in flight (the sum over s stays in split order).
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += 2 * stride) {
+    const long long j = i + stride;
+    const bool has_j = j < total;
+    const long long r0 = i / n4, c0 = (i % n4) * 4;
+    const long long r1 = has_j ? j / n4 : r0, c1 = has_j ? (j % n4) * 4 : c0;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+#pragma unroll 4
+    for (int s = 0; s < S; ++s) {
+      const float4 v0 = *reinterpret_cast<const float4*>(part + ((size_t)s * Mpad + r0) * N + c0);
+      const float4 v1 = *reinterpret_cast<const float4*>(part + ((size_t)s * Mpad + r1) * N + c1);
+      a0.x += v0.x;
+      a0.y += v0.y;
+      a0.z += v0.z;
+      a0.w += v0.w;
+      a1.x += v1.x;
+      a1.y += v1.y;
+      a1.z += v1.z;
+      a1.w += v1.w;
+    }
+    store(r0, c0, a0);
+    if (has_j) store(r1, c1, a1);
   }
 }
 
