@@ -205,6 +205,8 @@ def dh_sum_buffer(mesh: VocabMesh, rows: int, d: int, device: torch.device) -> D
     buf = _DH_BUFFERS.get(key)
     if buf is None or buf.rows < rows:
         grow = max(int(rows), -(-int(rows * 5 // 4) // 1024) * 1024)
+        if buf is not None:
+            torch.cuda.synchronize(device)  # no launch of this GPU still reads the old buffer
         _DH_BUFFERS.pop(key, None)
         buf = None
         try:
