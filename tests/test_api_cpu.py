@@ -153,3 +153,50 @@ def test_mesh_forward_routes_to_the_nvlink_exchange_or_the_all_gather(monkeypatc
     monkeypatch.setattr(losses, "stats_exchange", lambda m, rows, dev: None)
     assert losses._mesh_forward(W, H, y, 30.0, mesh, 6) == (logp, norm)
     assert calls == [("lp_fwd", 6, False), ("all_gather", mesh), ("lp_combine", (2, 3, 5))]
+
+
+def test_mesh_backward_routes_the_dh_sum(monkeypatch):
+    """The backward of a vocabulary mesh: with a multicast dH buffer, zeroed counters, a peer
+    barrier, the fused lp_bwd_sum backward and a second barrier (dH shared with the buffer);
+    without one, the plain backward and an all-reduce of dH. Device calls are stubbed; only
+    the routing and its order are checked."""
+    import torch
+
+    from gemma4_posttrain_jax_b200 import losses
+
+    calls = []
+    T, d, Vs = 6, 8, 10
+    H, y, g = torch.zeros(T, d), torch.zeros(T, dtype=torch.int32), torch.ones(T)
+    W, norm = torch.zeros(Vs, d), torch.ones(2, T)
+
+    class FakeMesh:
+        size = 2
+
+    class FakeBuf:
+        counters = torch.full((16,), 7, dtype=torch.int32)
+
+    def shard_backward(embed, Hz, yz, softcap, nz, gz, *, vocab_offset, need_dh, need_dw, dh_dtype, dw_dtype,
+                       token_chunk, dh_mesh_sum=None):
+        calls.append(("lp_bwd_sum" if dh_mesh_sum is not None else "lp_bwd", vocab_offset, dh_dtype))
+        return torch.zeros(T, d, dtype=dh_dtype), torch.zeros(Vs, d)
+
+    monkeypatch.setattr(losses.ops, "shard_backward", shard_backward)
+    monkeypatch.setattr(losses.ops, "bwd_sum_counters", lambda rows: 4)
+    monkeypatch.setattr(losses.ops, "peer_barrier", lambda buf, t: calls.append(("barrier", t)))
+    monkeypatch.setattr(losses, "all_reduce_sum", lambda t, m: calls.append(("all_reduce", t.dtype)) or t)
+    monkeypatch.setenv("LP_B200_PEER_TIMEOUT_MS", "777")
+    kw = dict(mesh=FakeMesh(), vocab_offset=10, need_dh=True, need_dw=True, dh_dtype=torch.bfloat16,
+              dw_dtype=torch.float32, token_chunk=None, skip_zero_grad=False)
+
+    buf = FakeBuf()
+    monkeypatch.setattr(losses, "dh_sum_buffer", lambda m, rows, dd, dev: buf)
+    dH, dW, pos, shared = losses._backward_rows(W, H, y, 30.0, norm, g, **kw)
+    assert shared and pos is None
+    assert calls == [("barrier", 777), ("lp_bwd_sum", 10, torch.bfloat16), ("barrier", 777)]
+    assert buf.counters[:4].eq(0).all() and buf.counters[4:].eq(7).all()  # the used counters are zeroed
+
+    calls.clear()
+    monkeypatch.setattr(losses, "dh_sum_buffer", lambda m, rows, dd, dev: None)
+    dH, dW, pos, shared = losses._backward_rows(W, H, y, 30.0, norm, g, **kw)
+    assert not shared
+    assert calls == [("lp_bwd", 10, torch.bfloat16), ("all_reduce", torch.bfloat16)]
