@@ -113,3 +113,68 @@ def test_sampler_argument_errors(cuda_device):
         sample_token(W, H, None, temperature=1.0, top_k=0, top_p=0.0)
     with pytest.raises(ValueError, match="log_probs"):
         ops.head(W, H, None, want_logits=False, log_probs=True)
+
+
+@pytest.mark.parametrize(
+    "temperature,top_k,top_p",
+    [(1.0, 0, 1.0), (0.7, 0, 1.0), (0.8, 3, 1.0), (0.8, 0, 0.85), (0.8, 4, 0.7), (0.8, 0, 1e-50)],
+)
+def test_sampling_distribution_matches_transformers_warpers(cuda_device, temperature, top_k, top_p):
+    """The reference's distribution test (``tests/test_sampler.py:175-205``): transformers'
+    temperature / top-k / top-p warpers give the expected distribution independently; 8192
+    draws per row must match it within 0.025 and never leave its support, and the recorded
+    logp is the untempered full log-softmax. The head reproduces the given logits exactly:
+    hidden = e_0 and W[v, 0] = logit (bf16-rounded)."""
+    from transformers.generation.logits_process import TemperatureLogitsWarper, TopKLogitsWarper, TopPLogitsWarper
+
+    from gemma4_posttrain_jax_b200 import sample_token
+
+    logits = orc.bf16_round(np.array([[1.1, -0.7, 0.3, 2.0, -2.0], [-1.0, 1.3, 0.6, -2.3, 0.1]], np.float32))
+    V, d, count = logits.shape[1], 8, 8192
+    gen = torch.Generator(device=cuda_device).manual_seed(128)
+    H = torch.zeros((count, d), dtype=torch.bfloat16, device=cuda_device)
+    H[:, 0] = 1.0
+    for row in range(2):
+        w = np.zeros((V, d), np.float32)
+        w[:, 0] = logits[row]
+        W = torch.from_numpy(w).to(cuda_device).to(torch.bfloat16)
+        scores = TemperatureLogitsWarper(temperature)(None, torch.from_numpy(logits[row : row + 1]))
+        if top_k:
+            scores = TopKLogitsWarper(top_k)(None, scores)
+        if top_p < 1:
+            scores = TopPLogitsWarper(top_p)(None, scores)
+        expected = torch.softmax(scores, dim=-1)[0].numpy()
+        raw = torch.log_softmax(torch.from_numpy(logits[row]).double(), dim=-1).numpy()
+        tokens, logps = sample_token(W, H, None, temperature=temperature, top_k=top_k, top_p=top_p, generator=gen)
+        t = tokens.cpu().numpy()
+        assert np.all(expected[t] > 0), "sampled a token outside the filtered support"
+        np.testing.assert_allclose(np.bincount(t, minlength=V) / count, expected, atol=0.025, rtol=0)
+        np.testing.assert_allclose(logps.cpu().numpy(), raw[t], atol=1e-5, rtol=0)
+
+
+def test_top_p_keeps_the_threshold_crossing_token(cuda_device):
+    """``tests/test_sampler.py:208-218``: probabilities (0.5, 0.3, 0.2) with top_p 0.6 keep the
+    first two columns (0.5 + 0.3 crosses 0.6), sampled 0.625 / 0.375."""
+    from gemma4_posttrain_jax_b200 import sample_token
+
+    V, d, count = 3, 8, 8192
+    w = np.zeros((V, d), np.float32)
+    w[:, 0] = orc.bf16_round(np.log(np.array([0.5, 0.3, 0.2], np.float32)))
+    W = torch.from_numpy(w).to(cuda_device).to(torch.bfloat16)
+    H = torch.zeros((count, d), dtype=torch.bfloat16, device=cuda_device)
+    H[:, 0] = 1.0
+    gen = torch.Generator(device=cuda_device).manual_seed(29)
+    tokens, _ = sample_token(W, H, None, temperature=1.0, top_k=0, top_p=0.6, generator=gen)
+    t = tokens.cpu().numpy()
+    assert set(t.tolist()) == {0, 1}
+    assert abs(float((t == 0).mean()) - 0.625) <= 0.025
+
+
+@pytest.mark.parametrize("top_p", [0.0, -0.5, 1.01, float("nan"), float("inf")])
+def test_invalid_top_p_is_rejected(cuda_device, top_p):
+    """``tests/test_sampler.py:221-228``."""
+    from gemma4_posttrain_jax_b200 import sample_token
+
+    _, _, W, H = _inputs(cuda_device, 2, 300, 64, 0.5, seed=2)
+    with pytest.raises(ValueError, match="top_p"):
+        sample_token(W, H, None, temperature=1.0, top_k=0, top_p=top_p)
