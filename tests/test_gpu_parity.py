@@ -436,3 +436,36 @@ def test_config3_and_config4_hidden_sizes(cuda_device, d, frozen_head):
         lp2_ref = orc.single_partition_logps(w2.float().numpy(), hn, y.numpy(), softcap=30.0, vocab_chunk=8192,
                                              sequence_chunk=128)
         assert np.abs(logp2.cpu().numpy() - lp2_ref).max() <= LOGP_ATOL
+
+
+def test_microbatched_completion_logps_match_the_full_batch(cuda_device):
+    """The reference's microbatch invariance (``tests/test_grpo.py:311-317``, atol / rtol
+    3e-6): completion logps of a batch equal those of its 2-row microbatches, and so do the
+    hidden-state gradients; dW summed over the microbatches matches the full batch's."""
+    from gemma4_posttrain_jax_b200.losses import completion_logps
+
+    rng = np.random.default_rng(5)
+    B, Pw, N, d, V = 6, 7, 150, 128, 3000
+    w = orc.bf16_round(rng.normal(size=(V, d)) * 0.3)
+    hidden = orc.bf16_round(rng.normal(size=(B, Pw + N, d)))
+    ids = rng.integers(0, V, size=(B, N)).astype(np.int32)
+    mask = np.arange(N)[None, :] < np.array([150, 40, 0, 77, 150, 3])[:, None]
+    adv = (rng.normal(size=(B, 1)) * (rng.random((B, N)) < 0.9)).astype(np.float32)
+    W = to_bf16(w, cuda_device).requires_grad_(True)
+    Hd = to_bf16(hidden, cuda_device).requires_grad_(True)
+    Y, M, G = (torch.from_numpy(x).to(cuda_device) for x in (ids, mask, adv))
+    full = completion_logps(W, Hd, Y, M, prompt_width=Pw, softcap=30.0)
+    (full * G).sum().backward()
+    dW_full, dH_full = W.grad.float().clone(), Hd.grad.float().clone()
+    W.grad = None
+    parts, dH_parts = [], []
+    for b0 in range(0, B, 2):
+        Hb = Hd.detach()[b0 : b0 + 2].clone().requires_grad_(True)
+        out = completion_logps(W, Hb, Y[b0 : b0 + 2], M[b0 : b0 + 2], prompt_width=Pw, softcap=30.0)
+        (out * G[b0 : b0 + 2]).sum().backward()
+        parts.append(out.detach())
+        dH_parts.append(Hb.grad.float())
+    split = torch.cat(parts).cpu().numpy()
+    np.testing.assert_allclose(split, full.detach().cpu().numpy(), atol=3e-6, rtol=3e-6)
+    assert rel_l2(torch.cat(dH_parts).cpu().numpy(), dH_full.cpu().numpy()) <= 5e-3
+    assert rel_l2(W.grad.float().cpu().numpy(), dW_full.cpu().numpy()) <= 1e-2
