@@ -149,7 +149,7 @@ struct Unit {
   int red_block;  // >= 0: a reduce item of this row block (no tiles)
 };
 
-__device__ __forceinline__ Unit get_unit(const GemmSched& s, int u) {
+__host__ __device__ __forceinline__ Unit get_unit(const GemmSched& s, int u) {
   int m, g, ks;
   if (s.red_lag > 0) {
     // tiles and reduce items interleaved (see red_lag); tiles in n_fast order
