@@ -183,7 +183,7 @@ def test_mesh_backward_routes_the_dh_sum(monkeypatch):
     monkeypatch.setattr(losses.ops, "shard_backward", shard_backward)
     monkeypatch.setattr(losses.ops, "bwd_sum_counters", lambda rows: 4)
     monkeypatch.setattr(losses.ops, "peer_barrier", lambda buf, t: calls.append(("barrier", t)))
-    monkeypatch.setattr(losses, "all_reduce_sum", lambda t, m: calls.append(("all_reduce", t.dtype)) or t)
+    monkeypatch.setattr(losses, "all_reduce_sum", lambda t, m: calls.append(("all_reduce", t.dtype, tuple(t.shape))) or t)
     monkeypatch.setenv("LP_B200_PEER_TIMEOUT_MS", "777")
     kw = dict(mesh=FakeMesh(), vocab_offset=10, need_dh=True, need_dw=True, dh_dtype=torch.bfloat16,
               dw_dtype=torch.float32, token_chunk=None, skip_zero_grad=False)
@@ -199,4 +199,7 @@ def test_mesh_backward_routes_the_dh_sum(monkeypatch):
     monkeypatch.setattr(losses, "dh_sum_buffer", lambda m, rows, dd, dev: None)
     dH, dW, pos, shared = losses._backward_rows(W, H, y, 30.0, norm, g, **kw)
     assert not shared
-    assert calls == [("lp_bwd", 10, torch.bfloat16), ("all_reduce", torch.bfloat16)]
+    # the only collective over tensor data is the [T, d] dH sum: the vocabulary-sharded
+    # embedding (and its gradient) never leaves its rank, as the reference asserts of its
+    # compiled program (tests/test_sharding_tpu.py:97-101)
+    assert calls == [("lp_bwd", 10, torch.bfloat16), ("all_reduce", torch.bfloat16, (T, d))]
