@@ -4,6 +4,7 @@ messages as the reference), no silent fallback, checkpoint identity (mirrors
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
@@ -203,3 +204,43 @@ def test_mesh_backward_routes_the_dh_sum(monkeypatch):
     # embedding (and its gradient) never leaves its rank, as the reference asserts of its
     # compiled program (tests/test_sharding_tpu.py:97-101)
     assert calls == [("lp_bwd", 10, torch.bfloat16), ("all_reduce", torch.bfloat16, (T, d))]
+
+
+@pytest.mark.parametrize(
+    "temperature,top_k,top_p",
+    [(1.0, 0, 1.0), (0.7, 0, 1.0), (0.8, 3, 1.0), (0.8, 0, 0.85), (0.8, 4, 0.7), (0.8, 0, 1e-50)],
+)
+def test_sampling_logic_matches_transformers_warpers_on_cpu(monkeypatch, temperature, top_k, top_p):
+    """sample_token's temperature / top-k / top-p / draw on top of the head, with the head
+    (lp_head) stubbed by exact logits so the logic runs on the CPU: frequencies match
+    transformers' warpers (the reference's test, tests/test_sampler.py:175-205) and the
+    recorded logp is the untempered log-softmax."""
+    import torch
+    from transformers.generation.logits_process import TemperatureLogitsWarper, TopKLogitsWarper, TopPLogitsWarper
+
+    from gemma4_posttrain_jax_b200 import sampler
+
+    logits = torch.tensor([1.1, -0.7, 0.3, 2.0, -2.0])
+    count = 20000
+
+    def head(embed, hidden, softcap, *, want_logits=True, log_probs=False):
+        z = logits.expand(hidden.shape[0], -1).clone()
+        m = z.max(dim=-1).values
+        norm = torch.stack([m, torch.exp(z - m[:, None]).sum(dim=-1)])
+        top = z.argmax(dim=-1).to(torch.int32)
+        return z, norm, top, z.max(dim=-1).values - (m + torch.log(norm[1]))
+
+    monkeypatch.setattr(sampler.ops, "head", head)
+    gen = torch.Generator().manual_seed(7)
+    tok, logp = sampler.sample_token(torch.zeros(5, 8), torch.zeros(count, 8), None, temperature=temperature,
+                                     top_k=top_k, top_p=top_p, generator=gen)
+    scores = TemperatureLogitsWarper(temperature)(None, logits[None])
+    if top_k:
+        scores = TopKLogitsWarper(top_k)(None, scores)
+    if top_p < 1:
+        scores = TopPLogitsWarper(top_p)(None, scores)
+    expected = torch.softmax(scores, dim=-1)[0].numpy()
+    t = tok.numpy()
+    assert (expected[t] > 0).all()
+    np.testing.assert_allclose(np.bincount(t, minlength=5) / count, expected, atol=0.02)
+    np.testing.assert_allclose(logp.numpy(), torch.log_softmax(logits, -1).numpy()[t], atol=1e-6)
