@@ -444,11 +444,17 @@ def main():
     _lib.profile_enable(True)
     phase_timer.enable(True)
     launches0 = _lib.launch_count()
+    try:
+        torch.cuda.reset_peak_memory_stats(dev)
+    except Exception:  # noqa: BLE001 - the peak is a reported extra, never a reason to fail
+        pass
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    step_marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with ClockSampler(list(range(world))) as clocks:
         start.record()
-        for _ in range(args.steps):
+        for i in range(args.steps):
             step(*inputs)
+            step_marks[i].record()
         stop.record()
         torch.cuda.synchronize()
     barrier()
@@ -460,6 +466,15 @@ def main():
     phase_timer.enable(False)
     ms = max_over_ranks(start.elapsed_time(stop) / args.steps)
     value = n_valid / (ms / 1e3)
+    # per-step device times and peak device memory of this rank (the reference's harness
+    # reports the mean, the p50 and the peak device bytes, bench.py:42-63)
+    try:
+        marks = [start, *step_marks]
+        per_step = [marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)]
+        step_stats = {"rank": rank, "p50_ms": float(np.median(per_step)), "min_ms": float(min(per_step)),
+                      "max_ms": float(max(per_step)), "peak_device_bytes": int(torch.cuda.max_memory_allocated(dev))}
+    except Exception:  # noqa: BLE001
+        step_stats = None
     clock_summary = clocks.summary() if rank == 0 else None
     assert _lib.device_error(local) == 0, "device-side error during the timed region"
 
@@ -600,6 +615,7 @@ def main():
             "kernels": kernels,
             "host_phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
             "kernel_ms_per_step": sum(v["ms_per_step"] for v in kernels.values()),
+            "step_stats": step_stats,
             "cta_group": cta_group_of_run(),
         }
         print(json.dumps(line), flush=True)
