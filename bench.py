@@ -4,17 +4,24 @@
 Workload (the metric's configuration): GRPO-shaped response-only
 logprob, forward + backward, tied LM head V=262144, d=2048, bf16, softcap 30. 128
 sequences of 2048 (512 prompt + 1536 response slots), response lengths uniform in
-[64, 1536], so ~102k valid response tokens per step; only those are computed
+[64, 1536], so ~108k valid response tokens per step; only those are computed
 (compaction). Upstream dlogp = per-sequence advantage ~ N(0,1) x Bernoulli(0.9) keep.
 The vocabulary is sharded over the N ranks (strong scaling: the global batch is fixed);
 hidden states / targets are replicated as at the reference's shard_map boundary, the
-per-token (max, sum, target) triples are all-gathered and merged, dH partials all-reduced.
+per-token (max, sum, target) triples are exchanged inside the forward and the dH partials
+summed inside the dH GEMM (NVLink multicast), or by NCCL where that is unavailable.
 
 A step = one call of the public API (``completion_logps``) + its backward on that batch:
 compaction, fused LM-head GEMM + online LSE, combine, recompute backward into dZ, dH and dW
 tensor-core GEMMs, scatter back. ``value`` has the inputs resident in HBM; ``e2e`` adds the
 host->device copy of every step's inputs (pinned; double-buffered, so step k+1's copy runs
 on the copy engines while step k computes) and the device->host read of the logps.
+
+After the timed regions one more step is checked against a PyTorch float32 reference of
+the same arithmetic computed on the GPUs (``parity``): the logp of every token, dH on 256
+sampled rows and dW on 256 sampled vocabulary rows of every shard, at the bars of the
+scope table (logp within 2e-3 absolute, dH / dW within 1e-2 relative L2). A failed check
+still prints the line, then exits with status 3.
 
 ``--impl reference`` times the CPU restatement of the reference's native path
 (``oracle/``; the reference itself is JAX-only and JAX is not installable here) on this
@@ -24,6 +31,7 @@ host's cores, on bounded samples of the same workload.
 from __future__ import annotations
 
 import argparse
+import datetime as _dt
 import json
 import os
 import subprocess
@@ -43,18 +51,21 @@ SOFTCAP = 30.0
 SEED = 0
 METRIC = "logprob fwd+bwd tokens/s @V=262144,d=2048 (GRPO response tokens, vocab-sharded)"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes (read + write) per launch of each GEMM on this workload at N=1, from one ncu
-# capture (profiles/dram_traffic_grpo_config2_1gpu.md); backward launches: an 8192-row chunk.
-NCU_TRAFFIC_PER_LAUNCH_N1 = {
-    "fwd_lse_gemm": 20.01e9,
-    "bwd_dz_gemm": 5.98e9,
-    "bwd_dh_gemm": 10.92e9,
-    "bwd_dw_gemm": 8.37e9,
-}
-
+# DRAM bytes (read + write) per launch of the forward GEMM on this workload at N=1: a stored
+# constant, not measured by this run. It comes from an ncu capture of the batch-16 case of
+# this workload (``ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum
+# --clock-control none -k regex:tc_gemm -c 1 python bench.py --batch 16 --steps 1
+# --warmup 3 --no-e2e --no-cpu-baseline --no-parity``), scaled by the tokens of the full
+# batch (traffic grows in proportion to the token count at a fixed vocabulary).
+NCU_FWD_TRAFFIC_PER_TOKEN_N1 = 20.01e9 / 108376
+NCU_TRAFFIC_NOTE = "stored constant: ncu DRAM bytes of the forward GEMM per token (batch-16 capture), x tokens"
+LOGP_ATOL, GRAD_RTOL = 2e-3, 1e-2
 
 # Dense-token BASELINE configs: (tokens, hidden, frozen head, extra forward-only pass).
-DENSE_CONFIGS = {1: (256, 2048, False, False), 3: (65536, 2560, False, True), 4: (32768, 3840, True, False)}
+DENSE_CONFIGS = {1: (256, 2048, False, False), 3: (65536, 2560, False, True), 4: (32768, 3840, True, False),
+                 5: (65536, 2048, False, False)}
+DENSE_NAMES = {1: "dense fwd+bwd", 3: "dense fwd+bwd + forward-only pass of W + N(0,1e-4)",
+               4: "dense fwd + dH, frozen head", 5: "dense fwd+bwd (T sweep)"}
 
 
 def parse_args():
@@ -65,18 +76,20 @@ def parse_args():
     p.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
     p.add_argument("--softcap", type=float, default=SOFTCAP, help="<= 0 disables the softcap")
     p.add_argument("--batch", type=int, default=B, help="sequences (default: config 2's 128)")
-    p.add_argument("--config", type=int, default=2, choices=(1, 2, 3, 4),
+    p.add_argument("--config", type=int, default=2, choices=(1, 2, 3, 4, 5),
                    help="BASELINE config: 2 = GRPO response tokens (the metric's workload, default); "
                         "1 = T=256 dense; 3 = T=65536, d=2560 + forward-only pass of a perturbed head; "
-                        "4 = T=32768, d=3840, frozen head (forward + dH)")
-    p.add_argument("--tokens", type=int, default=0, help="override T of configs 1 / 3 / 4")
+                        "4 = T=32768, d=3840, frozen head (forward + dH); 5 = dense d=2048 (T sweep)")
+    p.add_argument("--tokens", type=str, default="",
+                   help="T of configs 1 / 3 / 4 / 5; a comma-separated list runs each T in turn (one line each)")
     p.add_argument("--token-chunk", type=int, default=0, help="backward token chunk (0 = library default)")
     p.add_argument("--cta-group", type=int, default=0, choices=(0, 1, 2),
-                   help="tensor-core CTA group of the GEMMs (0 = library default, the CTA pair)")
+                   help="tensor-core CTA group of the GEMMs (0 = library default, per GEMM)")
     p.add_argument("--sampler-head", type=int, default=0, metavar="B",
                    help="instead: time the rollout sampler's LM head (lp_head) on B decode rows")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-parity", action="store_true", help="skip the float32 check of one step's results")
     return p.parse_args()
 
 
@@ -129,10 +142,14 @@ def cta_group_of_run():
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
+    """nvidia-smi samples (every 200 ms) of the GPUs' clocks and throttle reasons, started
+    before the warm-up so that samples exist for short timed regions; ``summary`` keeps the
+    samples that fall inside the marked windows."""
+
     FIELDS = (
-        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-        "clocks_event_reasons.sw_power_cap"
+        "timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
     )
 
     def __init__(self, indices):
@@ -140,7 +157,7 @@ class ClockSampler:
         self.proc = None
         self.file = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
@@ -152,42 +169,74 @@ class ClockSampler:
             self.proc = None
         return self
 
-    def __exit__(self, *exc):
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:  # noqa: BLE001
                 self.proc.kill()
+            self.proc = None
+        if self.file is not None:
+            self.file.close()
+            os.unlink(self.file.name)
+            self.file = None
 
-    def summary(self):
+    def _rows(self):
         if self.file is None:
-            return None
+            return []
         self.file.flush()
-        rows = [r.split(",") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
-        os.unlink(self.file.name)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            r = [x.strip() for x in r]
-            if len(r) < 9:
+        out = []
+        for line in Path(self.file.name).read_text().splitlines():
+            r = [x.strip() for x in line.split(",")]
+            if len(r) < 10:
                 continue
             try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
+                ts = _dt.datetime.strptime(r[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                out.append((ts, float(r[2]), float(r[3]), r[6:10]))
             except ValueError:
                 continue
-            for name, val in zip(names, r[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
+        return out
+
+    def summary(self, windows, since):
+        """Median SM clock and the active throttle reasons over the samples inside `windows`
+        ((start, end) wall-clock pairs); with fewer than two such samples (timed regions
+        shorter than the sampling period) over every sample since `since` (the warm-up)."""
+        rows = self._rows()
+        if not rows:
             return None
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(mx)), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        inside = [r for r in rows if any(a - 0.1 <= r[0] <= b + 0.1 for a, b in windows)]
+        window = "timed regions"
+        if len(inside) < 2:
+            inside = [r for r in rows if r[0] >= since]
+            window = "warm-up + timed regions"
+        if not inside:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in inside for n, v in zip(names, r[3]) if v.lower().startswith("active")})
+        return {"sm_mhz": float(np.median([r[1] for r in inside])), "sm_max_mhz": float(max(r[2] for r in inside)),
+                "reasons": reasons, "samples": len(inside), "window": window}
 
 
 # --------------------------------------------------------------------------- CPU baseline
-def blas_threads() -> int:
+def use_all_host_cores() -> int:
+    """Let numpy's BLAS use every core this process may run on (torchrun sets
+    OMP_NUM_THREADS=1 for its ranks); returns the thread count in effect."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover - non-Linux
+        n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=n, user_api="blas")
+    except Exception:  # noqa: BLE001
+        pass
+    torch.set_num_threads(n)
+    return blas_threads(default=n)
+
+
+def blas_threads(default: int | None = None) -> int:
     try:
         from threadpoolctl import threadpool_info
 
@@ -196,7 +245,10 @@ def blas_threads() -> int:
             return int(max(n))
     except Exception:  # noqa: BLE001
         pass
-    return os.cpu_count() or 1
+    return default or os.cpu_count() or 1
+
+
+CPU_SAMPLE_TOKENS = 256  # BASELINE config 1's T, taken from this workload's valid tokens
 
 
 def cpu_sample(W_host_f32, H_host, ids, mask, g, tokens, softcap):
@@ -226,17 +278,17 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    cores = use_all_host_cores()
     _, _, mask, ids, g = make_batch(args.batch)
     W, H = host_inputs(args.batch)
     Wf = W.float().numpy()
     Hf = H.float().numpy()
-    sample = 64
+    sample = CPU_SAMPLE_TOKENS
     for _ in range(args.warmup):
         cpu_sample(Wf, Hf, ids, mask, g, sample, args.softcap)
     secs = [cpu_sample(Wf, Hf, ids, mask, g, sample, args.softcap) for _ in range(args.steps)]
     per = float(np.mean(secs))
     value = sample / per
-    cores = blas_threads()
     n_valid = int(mask.sum())
     line = {
         "metric": METRIC,
@@ -258,8 +310,9 @@ def run_reference(args):
             "unit": "tokens/s",
             "cores": cores,
             "kind": "port",
-            "sample": f"{sample} valid response tokens per step (fwd+bwd over the full V=262144, d=2048), "
-            "numpy float32 restatement of losses.py:72-147 + its recompute backward",
+            "sample": f"{sample} valid response tokens of this workload per step (fwd+bwd over the full V=262144, "
+            "d=2048, the arithmetic of BASELINE config 1), numpy float32 restatement of losses.py:72-147 + its "
+            "recompute backward",
         },
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -318,108 +371,208 @@ def run_sampler_head(args):
     return 0
 
 
-# --------------------------------------------------------------------------- CUDA arm
-def main():
-    args = parse_args()
-    if args.impl == "reference":
-        return run_reference(args)
-    if args.sampler_head:
-        return run_sampler_head(args)
+# --------------------------------------------------------------------------- float32 parity check
+class Ranks:
+    """The collectives of the check (no-ops on one GPU); every rank makes the same calls."""
 
-    import torch.distributed as dist
+    def __init__(self, world: int):
+        self.world = world
 
-    from gemma4_posttrain_jax_b200 import _lib, build
+    def all_reduce(self, t: torch.Tensor, op: str) -> torch.Tensor:
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(t, op={"sum": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX}[op])
+        return t
+
+
+def parity_check(W, Hv, yv, gv, lp_v, dW, dHv, *, softcap, rank, world, dev, seed=1234, rows=256):
+    """Compare one step's results with a float32 PyTorch computation of the same math.
+
+    W: this rank's shard bf16 [Vs, d]; Hv bf16 [T, d], yv int [T] global ids, gv f32 [T]:
+    the tokens of the step; lp_v f32 [T], dW [Vs, d] (or None: frozen head), dHv [T, d]:
+    what the library returned. The reference forms every logit in float32 (exact bf16
+    products, float32 sums, as ``_matmul_f32``), the softcap, the log-sum-exp over every
+    shard, and from them the softmax-minus-one-hot gradients of sampled dH rows (over every
+    shard) and sampled dW rows (all tokens). Returns the error summary (same on every rank).
+    """
+    torch.set_float32_matmul_precision("highest")
+    ranks = Ranks(world)
+    T, d = Hv.shape
+    Vs = W.shape[0]
+    off = rank * Vs
+    Wf = W.detach().float()
+    cap = float(softcap) if softcap else None
+
+    def capped(z):
+        return cap * torch.tanh(z / cap) if cap else z
+
+    def chain(zc):  # d softcap / dz, from the capped value
+        return 1.0 - (zc / cap) ** 2 if cap else torch.ones_like(zc)
+
+    y_local = yv.to(torch.int64) - off
+    owned = (y_local >= 0) & (y_local < Vs)
+    m = torch.empty(T, device=dev)
+    s = torch.empty(T, device=dev)
+    tgt = torch.zeros(T, device=dev)
+    CH = max(256, min(8192, (1 << 30) // max(Vs, 1)))  # <= 4 GB of float32 logits per chunk
+    for t0 in range(0, T, CH):
+        t1 = min(T, t0 + CH)
+        z = capped(Hv[t0:t1].float() @ Wf.T)
+        mz = z.max(dim=1).values
+        m[t0:t1] = mz
+        s[t0:t1] = torch.exp(z - mz[:, None]).sum(dim=1)
+        li = y_local[t0:t1].clamp(0, Vs - 1)
+        tgt[t0:t1] = torch.where(owned[t0:t1], z.gather(1, li[:, None]).squeeze(1), torch.zeros_like(mz))
+        del z
+    m_g = ranks.all_reduce(m.clone(), "max")
+    s_g = ranks.all_reduce(s * torch.exp(m - m_g), "sum")
+    tgt_g = ranks.all_reduce(tgt, "sum")
+    lse = m_g + torch.log(s_g)
+    lp_ref = tgt_g - lse
+    e_lp = float((lp_v.float() - lp_ref).abs().max()) if T else 0.0
+
+    gen = torch.Generator(device=dev).manual_seed(seed)  # same draw on every rank
+    nz = torch.nonzero(gv != 0).squeeze(1)
+    R = nz[torch.randperm(nz.numel(), generator=gen, device=dev)[:rows]].sort().values
+    zR = capped(Hv[R].float() @ Wf.T)
+    oh = torch.zeros_like(zR)
+    rr = torch.nonzero(owned[R]).squeeze(1)
+    oh[rr, y_local[R][rr]] = 1.0
+    dz = gv[R][:, None] * (oh - torch.exp(zR - lse[R][:, None])) * chain(zR)
+    dH_ref = ranks.all_reduce(dz @ Wf, "sum")
+    dH_got = dHv[R].float()
+    e_dh = float(torch.linalg.norm(dH_got - dH_ref) / torch.linalg.norm(dH_ref)) if R.numel() else 0.0
+    zero_rows = torch.nonzero(gv == 0).squeeze(1)[:1024]
+    zero_ok = bool((dHv[zero_rows] == 0).all()) if zero_rows.numel() else True
+
+    e_dw = 0.0
+    if dW is not None:
+        genr = torch.Generator(device=dev).manual_seed(seed + 1 + rank)
+        tg = torch.unique(y_local[owned][:128])
+        extra = torch.randperm(Vs, generator=genr, device=dev)[: max(0, rows - tg.numel())]
+        C = torch.unique(torch.cat([tg, extra]))[:rows]
+        Hf = Hv.float()
+        zC = capped(Hf @ Wf[C].T)  # [T, |C|]
+        ohC = (y_local[:, None] == C[None, :]).float()
+        dzC = gv[:, None] * (ohC - torch.exp(zC - lse[:, None])) * chain(zC)
+        dW_ref = dzC.T @ Hf
+        e = torch.linalg.norm(dW[C].float() - dW_ref) / torch.linalg.norm(dW_ref)
+        e_dw = float(ranks.all_reduce(e.reshape(1).clone(), "max")[0])
+    e_lp = float(ranks.all_reduce(torch.tensor([e_lp], device=dev), "max")[0])
+    e_dh = float(ranks.all_reduce(torch.tensor([e_dh], device=dev), "max")[0])
+    ok = e_lp <= LOGP_ATOL and e_dh <= GRAD_RTOL and e_dw <= GRAD_RTOL and zero_ok
+    return {"logp_max_abs": e_lp, "dh_rel_l2": e_dh, "dw_rel_l2": e_dw if dW is not None else None,
+            "zero_grad_rows_zero": zero_ok, "tokens_checked": int(T), "dh_rows": int(R.numel()),
+            "dw_rows_per_shard": int(rows) if dW is not None else 0,
+            "bars": {"logp_abs": LOGP_ATOL, "grad_rel_l2": GRAD_RTOL},
+            "reference": "PyTorch float32 on the GPUs (exact bf16 products, float32 sums), every shard", "ok": ok}
+
+
+# --------------------------------------------------------------------------- workloads
+class Workload:
+    """One benchmark configuration: inputs, the step, FLOP counts and the parity view."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+def grpo_workload(args, dev, rank, world, mesh, softcap, chunk):
     from gemma4_posttrain_jax_b200.losses import completion_logps
-    from gemma4_posttrain_jax_b200.sharding import VocabMesh
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if not _lib.LIB_PATH.exists():
-        build.build()
-    _lib.load()
-    if args.cta_group:
-        _lib.set_cta_group(args.cta_group)
-    mesh = None
-    if world > 1:
-        from datetime import timedelta
+    prompt_len, resp_len, mask_np, ids_np, g_np = make_batch(args.batch)
+    n_valid = int(mask_np.sum())
+    # rows the backward computes: valid tokens with nonzero dlogp (zero-gradient rows are
+    # skipped by the library, as the reference's Pallas backward skips all-zero blocks)
+    n_bwd = int((g_np[mask_np] != 0).sum())
+    vs = V // world
+    # inputs: the same seeded draws on every rank; each rank keeps its W row block
+    gen = torch.Generator(device=dev).manual_seed(SEED + 1)
+    W_full = (torch.randn((V, D), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    W = W_full[rank * vs : (rank + 1) * vs].clone().requires_grad_(True)
+    del W_full
+    gen_h = torch.Generator(device=dev).manual_seed(SEED + 2)
+    H = torch.randn((args.batch, RESP, D), generator=gen_h, device=dev).to(torch.bfloat16)
+    ids = torch.from_numpy(ids_np).to(dev)
+    mask = torch.from_numpy(mask_np).to(dev)
+    g = torch.from_numpy(g_np).to(dev)
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-        mesh = VocabMesh(None)
+    def step(Hx, idsx, maskx, gx):
+        Hx = Hx.detach().requires_grad_(True)
+        lp = completion_logps(W, Hx, idsx, maskx, prompt_width=1, softcap=softcap, mesh=mesh, token_chunk=chunk,
+                              num_valid=n_valid)
+        dW, dH = torch.autograd.grad(lp, (W, Hx), gx)
+        return lp, dW, dH
 
-    softcap = args.softcap if args.softcap > 0 else None
-    chunk = args.token_chunk or None
+    def parity_view(out):
+        lp, dW, dH = out
+        extra_ok = bool((lp[~mask] == 0).all()) and bool((dH[~mask] == 0).all())
+        return dict(Hv=H[mask], yv=ids[mask], gv=g[mask], lp_v=lp[mask], dW=dW, dHv=dH[mask]), extra_ok
+
+    bwd = 2.0 * n_bwd * D * vs
+    return Workload(
+        W=W, inputs=[H, ids, mask, g], step=step, parity_view=parity_view, n_valid=n_valid, n_bwd=n_bwd, d=D, vs=vs,
+        flops={"fwd_lse_gemm": 2.0 * n_valid * D * vs, "bwd_dz_gemm": bwd, "bwd_dh_gemm": bwd, "bwd_dw_gemm": bwd},
+        total_flops=2.0 * n_valid * D * V + 6.0 * n_bwd * D * V, dense_flops=8.0 * n_valid * D * V,
+        out_shape=(args.batch, RESP), metric=METRIC, config=config_dict(args.batch, n_valid, world, args.softcap),
+        traffic_ok=world == 1 and args.batch == B and args.softcap == SOFTCAP)
+
+
+def dense_workload(args, dev, rank, world, mesh, softcap, chunk, T_cfg):
     from gemma4_posttrain_jax_b200.losses import per_token_logps
 
-    if args.config == 2:
-        d_model = D
-        prompt_len, resp_len, mask_np, ids_np, g_np = make_batch(args.batch)
-        n_valid = int(mask_np.sum())
-        # rows the backward computes: valid tokens with nonzero dlogp (zero-gradient rows are
-        # skipped by the library, as the reference's Pallas backward skips all-zero blocks)
-        n_bwd = int((g_np[mask_np] != 0).sum())
-        vs = V // world
-        # inputs: the same seeded draws on every rank; each rank keeps its W row block
-        gen = torch.Generator(device=dev).manual_seed(SEED + 1)
-        W_full = (torch.randn((V, D), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
-        W = W_full[rank * vs : (rank + 1) * vs].clone().requires_grad_(True)
-        del W_full
-        gen_h = torch.Generator(device=dev).manual_seed(SEED + 2)
-        H = torch.randn((args.batch, RESP, D), generator=gen_h, device=dev).to(torch.bfloat16).requires_grad_(True)
-        ids = torch.from_numpy(ids_np).to(dev)
-        mask = torch.from_numpy(mask_np).to(dev)
-        g = torch.from_numpy(g_np).to(dev)
-        inputs = [H.detach(), ids, mask, g]
-        fwd_launch_flops = 2.0 * n_valid * D * vs
-        bwd_launch_flops = {"bwd_dz_gemm": 2.0 * n_bwd * D * vs, "bwd_dh_gemm": 2.0 * n_bwd * D * vs,
-                            "bwd_dw_gemm": 2.0 * n_bwd * D * vs}
-        total_flops_needed = 2.0 * n_valid * D * V + 6.0 * n_bwd * D * V
-        dense_flops = 8.0 * n_valid * D * V
+    _, d_model, frozen, second_pass = DENSE_CONFIGS[args.config]
+    vs = V // world
+    gen = torch.Generator(device=dev).manual_seed(SEED + 1)
+    W_full = (torch.randn((V, d_model), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    W = W_full[rank * vs : (rank + 1) * vs].clone().requires_grad_(not frozen)
+    W2 = None
+    if second_pass:  # old / reference policy head: W + N(0, 1e-4)
+        W2 = (W.detach().float() + torch.randn(W.shape, generator=gen, device=dev) * 1e-4).to(torch.bfloat16)
+    del W_full
+    gen_h = torch.Generator(device=dev).manual_seed(SEED + 2)
+    Hd = torch.randn((T_cfg, d_model), generator=gen_h, device=dev).to(torch.bfloat16)
+    Yd = torch.randint(0, V, (T_cfg,), generator=gen_h, device=dev, dtype=torch.int32)
+    Gd = torch.randn((T_cfg,), generator=gen_h, device=dev)
 
-        def step(Hx, idsx, maskx, gx):
-            Hx = Hx.detach().requires_grad_(True)
-            lp = completion_logps(W, Hx, idsx, maskx, prompt_width=1, softcap=softcap, mesh=mesh, token_chunk=chunk,
-                                  num_valid=n_valid)
-            dW, dH = torch.autograd.grad(lp, (W, Hx), gx)
-            return lp, dW, dH
-    else:
-        T_cfg, d_model, frozen, second_pass = DENSE_CONFIGS[args.config]
-        T_cfg = args.tokens or T_cfg
-        n_valid = n_bwd = T_cfg
-        vs = V // world
-        gen = torch.Generator(device=dev).manual_seed(SEED + 1)
-        W_full = (torch.randn((V, d_model), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
-        W = W_full[rank * vs : (rank + 1) * vs].clone().requires_grad_(not frozen)
-        W2 = None
-        if second_pass:  # old / reference policy head: W + N(0, 1e-4)
-            W2 = (W.detach().float() + torch.randn(W.shape, generator=gen, device=dev) * 1e-4).to(torch.bfloat16)
-        del W_full
-        gen_h = torch.Generator(device=dev).manual_seed(SEED + 2)
-        Hd = torch.randn((T_cfg, d_model), generator=gen_h, device=dev).to(torch.bfloat16)
-        Yd = torch.randint(0, V, (T_cfg,), generator=gen_h, device=dev, dtype=torch.int32)
-        Gd = torch.randn((T_cfg,), generator=gen_h, device=dev)
-        inputs = [Hd, Yd, Gd]
-        fwd_launch_flops = 2.0 * T_cfg * d_model * vs
-        bwd_launch_flops = {"bwd_dz_gemm": 2.0 * T_cfg * d_model * vs, "bwd_dh_gemm": 2.0 * T_cfg * d_model * vs}
-        if not frozen:
-            bwd_launch_flops["bwd_dw_gemm"] = 2.0 * T_cfg * d_model * vs
-        total_flops_needed = (2.0 * (2 if second_pass else 1) + (4.0 if frozen else 6.0)) * T_cfg * d_model * V
-        dense_flops = total_flops_needed
+    def step(Hx, Yx, Gx):
+        Hx = Hx.detach().requires_grad_(True)
+        lp = per_token_logps(W, Hx, Yx, softcap=softcap, mesh=mesh, token_chunk=chunk)
+        if frozen:
+            (dH,) = torch.autograd.grad(lp, (Hx,), Gx)
+            dW = None
+        else:
+            dW, dH = torch.autograd.grad(lp, (W, Hx), Gx)
+        if W2 is not None:
+            with torch.no_grad():
+                per_token_logps(W2, Hx.detach(), Yx, softcap=softcap, mesh=mesh)
+        return lp, dW, dH
 
-        def step(Hx, Yx, Gx):
-            Hx = Hx.detach().requires_grad_(True)
-            lp = per_token_logps(W, Hx, Yx, softcap=softcap, mesh=mesh, token_chunk=chunk)
-            wrt = (Hx,) if frozen else (W, Hx)
-            grads = torch.autograd.grad(lp, wrt, Gx)
-            if W2 is not None:
-                with torch.no_grad():
-                    lp2 = per_token_logps(W2, Hx.detach(), Yx, softcap=softcap, mesh=mesh)
-                return lp, lp2, grads
-            return lp, grads
+    def parity_view(out):
+        lp, dW, dH = out
+        return dict(Hv=Hd, yv=Yd, gv=Gd, lp_v=lp, dW=dW, dHv=dH), True
+
+    flops = {"fwd_lse_gemm": 2.0 * T_cfg * d_model * vs * (2 if second_pass else 1),
+             "bwd_dz_gemm": 2.0 * T_cfg * d_model * vs, "bwd_dh_gemm": 2.0 * T_cfg * d_model * vs}
+    if not frozen:
+        flops["bwd_dw_gemm"] = 2.0 * T_cfg * d_model * vs
+    total = (2.0 * (2 if second_pass else 1) + (4.0 if frozen else 6.0)) * T_cfg * d_model * V
+    cfg = {"workload": f"BASELINE config {args.config}: {DENSE_NAMES[args.config]}", "tokens": T_cfg,
+           "hidden": d_model, "vocab": V, "vocab_per_gpu": vs, "softcap": args.softcap if args.softcap > 0 else None,
+           "parallelism": f"vocab{world}", "l2": "no flush: W shard exceeds the 126 MB L2"}
+    return Workload(
+        W=W, inputs=[Hd, Yd, Gd], step=step, parity_view=parity_view, n_valid=T_cfg, n_bwd=T_cfg, d=d_model, vs=vs,
+        flops=flops, total_flops=total, dense_flops=total, out_shape=(T_cfg,),
+        metric=f"logprob tokens/s @V=262144,d={d_model} (BASELINE config {args.config}, vocab-sharded)", config=cfg,
+        traffic_ok=False)
+
+
+# --------------------------------------------------------------------------- CUDA arm
+def measure(args, wl, *, dev, rank, world, local, clocks):
+    """Warm-up, device-resident timing, end-to-end timing, parity, roofline; the JSON line."""
+    import torch.distributed as dist
+
+    from gemma4_posttrain_jax_b200 import _lib, phase_timer
 
     def barrier():
         if world > 1:
@@ -432,31 +585,32 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---------------------------------------------------------------- device-resident timing
+    windows = []
+    t_warm = time.time()
     for _ in range(args.warmup):
-        step(*inputs)
+        wl.step(*wl.inputs)
     torch.cuda.synchronize()
     assert _lib.device_error(local) == 0, "device-side error during warm-up"
     barrier()
     torch.cuda.synchronize()
-    from gemma4_posttrain_jax_b200 import phase_timer
+    free0, total_mem = torch.cuda.mem_get_info(dev)
 
+    # ---------------------------------------------------------------- device-resident timing
     _lib.profile_enable(True)
     phase_timer.enable(True)
     launches0 = _lib.launch_count()
-    try:
-        torch.cuda.reset_peak_memory_stats(dev)
-    except Exception:  # noqa: BLE001 - the peak is a reported extra, never a reason to fail
-        pass
+    torch.cuda.reset_peak_memory_stats(dev)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     step_marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(list(range(world))) as clocks:
-        start.record()
-        for i in range(args.steps):
-            step(*inputs)
-            step_marks[i].record()
-        stop.record()
-        torch.cuda.synchronize()
+    t_wall0 = time.time()
+    start.record()
+    for i in range(args.steps):
+        wl.step(*wl.inputs)
+        step_marks[i].record()
+    stop.record()
+    torch.cuda.synchronize()
+    windows.append((t_wall0, time.time()))
+    free1, _ = torch.cuda.mem_get_info(dev)
     barrier()
     torch.cuda.synchronize()
     launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
@@ -465,17 +619,15 @@ def main():
     phases = phase_timer.read()
     phase_timer.enable(False)
     ms = max_over_ranks(start.elapsed_time(stop) / args.steps)
-    value = n_valid / (ms / 1e3)
-    # per-step device times and peak device memory of this rank (the reference's harness
-    # reports the mean, the p50 and the peak device bytes, bench.py:42-63)
-    try:
-        marks = [start, *step_marks]
-        per_step = [marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)]
-        step_stats = {"rank": rank, "p50_ms": float(np.median(per_step)), "min_ms": float(min(per_step)),
-                      "max_ms": float(max(per_step)), "peak_device_bytes": int(torch.cuda.max_memory_allocated(dev))}
-    except Exception:  # noqa: BLE001
-        step_stats = None
-    clock_summary = clocks.summary() if rank == 0 else None
+    value = wl.n_valid / (ms / 1e3)
+    # per-step device times and device memory of this rank (the reference's harness reports
+    # the mean, the p50 and the peak device bytes, bench.py:42-63)
+    marks = [start, *step_marks]
+    per_step = [marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)]
+    step_stats = {"rank": rank, "p50_ms": float(np.median(per_step)), "min_ms": float(min(per_step)),
+                  "max_ms": float(max(per_step)),
+                  "torch_peak_allocated_bytes": int(torch.cuda.max_memory_allocated(dev)),
+                  "device_used_bytes": int(total_mem - min(free0, free1))}
     assert _lib.device_error(local) == 0, "device-side error during the timed region"
 
     # ---------------------------------------------------------------- end-to-end (host buffers)
@@ -484,10 +636,9 @@ def main():
         # Every step copies its inputs from pinned host memory and reads its logps back. The
         # inputs are double-buffered: step k+1's host->device copies run on a copy stream
         # (copy engines) while step k computes, as a data loader would feed the trainer.
-        hosts = [x.detach().cpu().pin_memory() for x in inputs]
-        bufs = [[torch.empty_like(x) for x in inputs] for _ in range(2)]
-        out_shape = (args.batch, RESP) if args.config == 2 else (n_valid,)
-        out_host = torch.empty(out_shape, dtype=torch.float32).pin_memory()
+        hosts = [x.detach().cpu().pin_memory() for x in wl.inputs]
+        bufs = [[torch.empty_like(x) for x in wl.inputs] for _ in range(2)]
+        out_host = torch.empty(wl.out_shape, dtype=torch.float32).pin_memory()
         h2d = sum(x.nbytes for x in hosts)
         d2h = out_host.nbytes
         copy_stream = torch.cuda.Stream(dev)
@@ -511,7 +662,7 @@ def main():
                 if k + 1 < nsteps:
                     issue_copy(k + 1)
                 torch.cuda.current_stream().wait_event(copied[b])
-                out = step(*bufs[b])
+                out = wl.step(*bufs[b])
                 compute_done[b].record()
                 out_host.copy_(out[0].detach(), non_blocking=True)
 
@@ -520,35 +671,52 @@ def main():
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t_wall0 = time.time()
         e0.record()
         e2e_run(args.steps)
         e1.record()
         torch.cuda.synchronize()
+        windows.append((t_wall0, time.time()))
         barrier()
         ems = max_over_ranks(e0.elapsed_time(e1) / args.steps)
-        e2e = {"value": n_valid / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems, "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(d2h)}
+        e2e = {"value": wl.n_valid / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+        del hosts, bufs
+
+    # ---------------------------------------------------------------- parity of one step
+    parity = None
+    if not args.no_parity:
+        out = wl.step(*wl.inputs)
+        view, extra_ok = wl.parity_view(out)
+        parity = parity_check(wl.W, softcap=args.softcap if args.softcap > 0 else None, rank=rank, world=world,
+                              dev=dev, **view)
+        parity["masked_slots_zero"] = extra_ok
+        parity["ok"] = bool(parity["ok"] and extra_ok)
+        del out, view
+        torch.cuda.empty_cache()
+        assert _lib.device_error(local) == 0, "device-side error in the parity step"
 
     # ---------------------------------------------------------------- roofline of the dominant kernel
     peaks, peak_src = load_peaks()
-    n_fwd_passes = 2 if (args.config == 3) else 1
-    flops_per_step = {"fwd_lse_gemm": fwd_launch_flops * n_fwd_passes, **bwd_launch_flops}
     kernels = {}
     for name, (tot_ms, cnt) in prof.items():
         per_launch = tot_ms / max(cnt, 1)
         entry = {"launches_per_step": cnt / args.steps, "ms_per_step": tot_ms / args.steps, "ms_per_launch": per_launch}
-        if name in flops_per_step:
-            tf = flops_per_step[name] * args.steps / (tot_ms / 1e3) / 1e12
+        if name in wl.flops:
+            tf = wl.flops[name] * args.steps / (tot_ms / 1e3) / 1e12
             entry["tflops"] = tf
             entry["frac_of_sustained_peak"] = tf / peaks["bf16_tflops_sustained"]
         kernels[name] = entry
-    gemm_names = [k for k in kernels if k in flops_per_step]
+    gemm_names = [k for k in kernels if k in wl.flops]
     dom = max(gemm_names, key=lambda k: kernels[k]["ms_per_step"]) if gemm_names else None
     roofline = None
     if dom is not None:
         cnt = prof[dom][1]
-        flop_per_launch = flops_per_step[dom] * args.steps / max(cnt, 1)
+        flop_per_launch = wl.flops[dom] * args.steps / max(cnt, 1)
         achieved = flop_per_launch / (kernels[dom]["ms_per_launch"] / 1e3) / 1e12
+        traffic = None
+        if wl.traffic_ok and dom == "fwd_lse_gemm":
+            traffic = NCU_FWD_TRAFFIC_PER_TOKEN_N1 * wl.n_valid
         roofline = {
             "kernel": dom,
             "bound": "tensor",
@@ -556,41 +724,57 @@ def main():
             "peak": peaks["bf16_tflops_sustained"],
             "unit": "TFLOP/s",
             "frac": achieved / peaks["bf16_tflops_sustained"],
-            "traffic": (NCU_TRAFFIC_PER_LAUNCH_N1.get(dom)
-                        if world == 1 and args.config == 2 and args.batch == B and args.softcap == SOFTCAP else None),
-            "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+            "traffic": traffic,
+            "traffic_unit": "bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum)",
+            "traffic_source": NCU_TRAFFIC_NOTE if traffic is not None else None,
             "peak_source": f"bf16_tflops_sustained ({peak_src}); kernel runs inside a long step",
             "flop_per_launch": flop_per_launch,
         }
-    step_tflops = total_flops_needed / (ms / 1e3) / 1e12  # the GEMM work one step needs
-    dense_equiv_tflops = dense_flops / (ms / 1e3) / 1e12  # the 8*T*d*V roofline's count (config 2)
+    step_tflops = wl.total_flops / (ms / 1e3) / 1e12  # the GEMM work one step needs
+    dense_equiv_tflops = wl.dense_flops / (ms / 1e3) / 1e12
+
+    # ---------------------------------------------------------------- exposed collective time
+    def kms(name):
+        return kernels[name]["ms_per_step"] if name in kernels else 0.0
+
+    collective = None
+    if world > 1:
+        dh_over = 0.0
+        if "bwd_dh_gemm" in kernels and "bwd_dw_gemm" in kernels:
+            # the dH GEMM's time above the rate of this run's dW GEMM (same FLOPs, same CTA-pair
+            # tiling, no collective): the cost of the dH sum inside it
+            dw_rate = wl.flops["bwd_dw_gemm"] / kms("bwd_dw_gemm")
+            dh_over = max(0.0, kms("bwd_dh_gemm") - wl.flops["bwd_dh_gemm"] / dw_rate)
+        nccl = sum(v[0] for k, v in phases.items() if k in ("stats_all_gather", "dh_all_reduce")) / args.steps
+        parts = {"fwd_exchange_ms": kms("fwd_finalize_mesh"), "peer_barrier_ms": kms("peer_barrier"),
+                 "nccl_ms": nccl, "dh_sum_in_gemm_ms_est": dh_over}
+        total = sum(parts.values())
+        collective = {**parts, "exposed_collective_ms": total, "frac_of_step": total / ms,
+                      "note": "fwd_exchange includes the wait for the slowest rank's forward GEMM"}
 
     # ---------------------------------------------------------------- CPU baseline (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == 2:
-        Wf = W.detach().float().cpu().numpy()
-        Hf = H.detach().float().cpu().numpy()
-        sample = 64
+        cores = use_all_host_cores()
+        Wf = wl.W.detach().float().cpu().numpy()
+        Hf = wl.inputs[0].float().cpu().numpy()
+        mask_np = wl.inputs[2].cpu().numpy()
+        ids_np = wl.inputs[1].cpu().numpy()
+        g_np = wl.inputs[3].cpu().numpy()
+        sample = CPU_SAMPLE_TOKENS
         t = cpu_sample(Wf, Hf, ids_np, mask_np, g_np, sample, args.softcap)
-        if t < 4.0:
-            sample = 256
-            t = cpu_sample(Wf, Hf, ids_np, mask_np, g_np, sample, args.softcap)
-        cpu = {"value": sample / t, "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
+        cpu = {"value": sample / t, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{sample} valid response tokens of this workload, fwd+bwd over V=262144, d=2048 "
                f"({t:.1f} s), numpy float32 restatement of losses.py:72-147 + recompute backward"}
+        del Wf, Hf
 
+    clock_summary = None
     if rank == 0:
-        metric = METRIC if args.config == 2 else (
-            f"logprob tokens/s @V=262144,d={d_model} (BASELINE config {args.config}, vocab-sharded)")
-        cfg = config_dict(args.batch, n_valid, world, args.softcap) if args.config == 2 else {
-            "workload": f"BASELINE config {args.config}: "
-            + {1: "dense fwd+bwd", 3: "dense fwd+bwd + forward-only pass of W + N(0,1e-4)",
-               4: "dense fwd + dH, frozen head"}[args.config],
-            "tokens": n_valid, "hidden": d_model, "vocab": V, "vocab_per_gpu": vs,
-            "softcap": args.softcap if args.softcap > 0 else None, "parallelism": f"vocab{world}",
-            "l2": "no flush: W shard exceeds the 126 MB L2"}
+        clock_summary = clocks.summary(windows, t_warm)
+    line = None
+    if rank == 0:
         line = {
-            "metric": metric,
+            "metric": wl.metric,
             "value": value,
             "unit": "tokens/s",
             "n_gpus": world,
@@ -602,16 +786,19 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) hidden, N(0,0.02) W, uniform targets)",
-            "config": cfg,
+            "config": wl.config,
             "clocks": clock_summary,
+            "sm_mcycles_per_step": (ms * clock_summary["sm_mhz"] / 1e3) if clock_summary else None,
             "e2e": e2e,
             "gpu_launches": int(launches),
             "roofline": roofline,
             "cpu_baseline": cpu,
+            "parity": parity,
+            "collective": collective,
             "step_tflops": step_tflops,
             "step_frac_of_sustained_peak": step_tflops / world / peaks["bf16_tflops_sustained"],
             "dense_8Tdv_tflops": dense_equiv_tflops,
-            "backward_rows": n_bwd,
+            "backward_rows": wl.n_bwd,
             "kernels": kernels,
             "host_phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
             "kernel_ms_per_step": sum(v["ms_per_step"] for v in kernels.values()),
@@ -619,9 +806,62 @@ def main():
             "cta_group": cta_group_of_run(),
         }
         print(json.dumps(line), flush=True)
+    return parity is None or parity["ok"]
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.sampler_head:
+        return run_sampler_head(args)
+
+    import torch.distributed as dist
+
+    from gemma4_posttrain_jax_b200 import _lib, build
+    from gemma4_posttrain_jax_b200.sharding import VocabMesh
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if not _lib.LIB_PATH.exists():
+        build.build()
+    _lib.load()
+    if args.cta_group:
+        _lib.set_cta_group(args.cta_group)
+    mesh = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        mesh = VocabMesh(None)
+
+    softcap = args.softcap if args.softcap > 0 else None
+    chunk = args.token_chunk or None
+    clocks = ClockSampler(list(range(world)))
+    if rank == 0:
+        clocks.start()
+    ok = True
+    try:
+        if args.config == 2:
+            ok = measure(args, grpo_workload(args, dev, rank, world, mesh, softcap, chunk), dev=dev, rank=rank,
+                         world=world, local=local, clocks=clocks)
+        else:
+            tokens = [int(t) for t in args.tokens.split(",") if t.strip()] or [DENSE_CONFIGS[args.config][0]]
+            for T_cfg in tokens:
+                wl = dense_workload(args, dev, rank, world, mesh, softcap, chunk, T_cfg)
+                ok = measure(args, wl, dev=dev, rank=rank, world=world, local=local, clocks=clocks) and ok
+                del wl
+                torch.cuda.empty_cache()
+    finally:
+        clocks.stop()
     if world > 1:
         dist.destroy_process_group()
-    return 0
+    return 0 if ok else 3
 
 
 if __name__ == "__main__":

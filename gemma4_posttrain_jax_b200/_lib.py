@@ -34,6 +34,7 @@ _SIG = {
     "lp_last_error": (ctypes.c_char_p, []),
     "lp_launch_count": (ctypes.c_longlong, []),
     "lp_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "lp_device_error_poll": (ctypes.c_int, [ctypes.c_int]),
     "lp_set_cta_group": (ctypes.c_int, [ctypes.c_int]),
     "lp_get_cta_group": (ctypes.c_int, []),
     "lp_device_pairs": (ctypes.c_int, []),
@@ -131,6 +132,41 @@ def device_error(device: int) -> int:
     code = ctypes.c_int(0)
     check(load().lp_device_error(device, ctypes.byref(code)), "lp_device_error")
     return code.value
+
+
+# Device-side error codes (lp_ptx.cuh): which bounded wait gave up.
+DEVICE_ERROR_NAMES = {
+    1: "DEV_TIMEOUT_PRODUCER (a GEMM's TMA producer waited too long for a free stage)",
+    2: "DEV_TIMEOUT_MMA (a GEMM's MMA issuer waited too long for its operands)",
+    3: "DEV_TIMEOUT_EPILOGUE (a GEMM's epilogue waited too long for its accumulator)",
+    4: "DEV_TIMEOUT_DRAIN (a GEMM could not drain its loads or MMAs)",
+    5: "DEV_TIMEOUT_PEER (another rank of the vocabulary mesh did not arrive in time)",
+}
+
+
+class DeviceTimeoutError(LogprobLibraryError):
+    """A kernel of the library gave up a bounded wait; its outputs are not valid."""
+
+
+def device_error_poll(device: int) -> int:
+    """The device-side error code of ``device`` without a CUDA call or synchronisation
+    (covers the kernels that have completed; 0 = none since the last ``device_error``)."""
+    return int(load().lp_device_error_poll(int(device)))
+
+
+def raise_on_device_error(device: int, where: str) -> None:
+    """Raise ``DeviceTimeoutError`` if a kernel recorded a device-side error on ``device``.
+
+    Reads the host-mapped copy of the code (no synchronisation): call it after waiting for
+    the stream whose kernels it should cover. The code stays set until ``device_error``
+    clears it, so every later check raises too."""
+    code = device_error_poll(device)
+    if code:
+        raise DeviceTimeoutError(
+            f"{where}: a kernel on cuda:{device} recorded device error {code}: "
+            f"{DEVICE_ERROR_NAMES.get(code, 'unknown code')}; its outputs are not valid "
+            "(read and clear the code with _lib.device_error before retrying)"
+        )
 
 
 def profile_enable(on: bool = True) -> None:

@@ -179,6 +179,25 @@ int max_resident_pairs(int sms, int* pairs) {
   return LP_OK;
 }
 
+// Host-visible device error codes: one int per device in mapped, pinned host memory, which
+// kernels write (besides g_lp_device_error) when they record an error. Reading a slot is a
+// plain host load, so callers can check for errors at points where they already wait for
+// the GPU without another synchronisation.
+int* g_host_errors = nullptr;  // [kMaxDevices], allocated on the first device set-up
+
+int setup_host_error_mirror(int dev) {
+  if (g_host_errors == nullptr) {
+    void* p = nullptr;
+    LP_CUDA_TRY(cudaHostAlloc(&p, kMaxDevices * sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable));
+    std::memset(p, 0, kMaxDevices * sizeof(int));
+    g_host_errors = static_cast<int*>(p);
+  }
+  int* dptr = nullptr;
+  LP_CUDA_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&dptr), g_host_errors + dev, 0));
+  LP_CUDA_TRY(cudaMemcpyToSymbol(g_lp_host_error, &dptr, sizeof(dptr)));
+  return LP_OK;
+}
+
 int current_device_info(DeviceInfo** out) {
   int dev = 0;
   LP_CUDA_TRY(cudaGetDevice(&dev));
@@ -193,6 +212,7 @@ int current_device_info(DeviceInfo** out) {
     if (d.major == 10 && d.minor == 0) {
       int rc = max_resident_pairs(d.sms, &d.pairs);
       if (rc) return rc;
+      if ((rc = setup_host_error_mirror(dev))) return rc;
     }
     d.ready = true;
   }
@@ -369,12 +389,21 @@ GemmSched plan_gemm(int64_t M, int64_t N, int64_t K, int sms, bool allow_split, 
   return s;
 }
 
+// Backward token chunk: dZ (bf16 [chunk, Vs]) is the backward's only [T, V]-shaped buffer,
+// so its size bounds the chunk (LP_B200_DZ_CHUNK_MB, default 4096 MB). Chunks are of equal
+// size on 256-row boundaries: a short last chunk leaves most SMs idle at the end of each of
+// its three GEMMs.
 int64_t default_token_chunk(int64_t T, int64_t Vs) {
+  static const int64_t budget = [] {
+    const char* e = getenv("LP_B200_DZ_CHUNK_MB");
+    const long long mb = (e != nullptr && atoll(e) > 0) ? atoll(e) : 4096;
+    return (int64_t)mb << 20;
+  }();
   const int64_t ldz = (Vs + 7) / 8 * 8;
-  const int64_t budget = int64_t(4) << 30;  // bytes of bf16 dZ per chunk
-  int64_t tc = budget / (ldz * 2);
-  tc = std::max<int64_t>(256, tc / 256 * 256);
-  return std::min<int64_t>(tc, std::max<int64_t>(T, 1));
+  const int64_t cap = std::max<int64_t>(256, budget / (ldz * 2) / 256 * 256);
+  if (T <= cap) return std::max<int64_t>(T, 1);
+  const int64_t chunks = cdiv(T, cap);
+  return std::min<int64_t>(cap, cdiv(cdiv(T, chunks), 256) * 256);
 }
 
 struct BwdLayout {
@@ -649,8 +678,17 @@ int lp_device_error(int device, int* code) {
   if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_lp_device_error, &zero, sizeof(int));
   cudaSetDevice(prev);
   if (e != cudaSuccess) return fail(LP_ECUDA, "lp_device_error: %s", cudaGetErrorString(e));
+  if (g_host_errors != nullptr && device >= 0 && device < kMaxDevices) {
+    if (v == 0) v = reinterpret_cast<volatile int*>(g_host_errors)[device];
+    reinterpret_cast<volatile int*>(g_host_errors)[device] = 0;
+  }
   if (code) *code = v;
   return LP_OK;
+}
+
+int lp_device_error_poll(int device) {
+  if (device < 0 || device >= kMaxDevices || g_host_errors == nullptr) return 0;
+  return reinterpret_cast<volatile int*>(g_host_errors)[device];
 }
 
 size_t lp_fwd_workspace_bytes(int64_t T, int64_t Vs) {
@@ -862,6 +900,8 @@ int lp_combine(void* stream, const float* shard_stats, int P, int64_t T, float* 
   if (P <= 0 || T < 0) return fail(LP_EINVAL, "bad P=%d or T=%lld", P, (long long)T);
   if (T == 0) return LP_OK;
   if (shard_stats == nullptr) return fail(LP_EINVAL, "null shard_stats");
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device_info(&di)) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   ProfScope prof(st, "combine");
   combine_kernel<<<(unsigned)cdiv(T, 256), 256, 0, st>>>(shard_stats, P, (int)T, logp, norm);
@@ -973,6 +1013,7 @@ int bwd_impl(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, con
         p.s.red_lag = std::min(p.s.tiles_m, (int)cdiv(3 * (int64_t)wk, p.s.tiles_n) + 2);
         p.s.num_units = p.s.tiles_m * p.s.tiles_n + p.s.tiles_m;
         p.e.sum_mc = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(ms->dh_mc) + (size_t)t0 * ld_dh * 2);
+        p.e.sum_local = reinterpret_cast<__nv_bfloat16*>(dh_c);
         p.e.sum_ld = ld_dh;
         p.e.cnt_local = ms->cnt_local + t0 / 128;
         p.e.cnt_mc = ms->cnt_mc + t0 / 128;
@@ -1123,6 +1164,8 @@ int lp_compact(void* stream, const uint8_t* mask, int64_t B, int64_t N, const vo
   const size_t need = lp_compact_workspace_bytes(B, N);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(LP_EWORKSPACE, "lp_compact needs %zu workspace bytes, got %zu", need, workspace_bytes);
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device_info(&di)) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (slots == 0) {
     LP_CUDA_TRY(cudaMemsetAsync(count, 0, sizeof(int32_t), st));
@@ -1139,9 +1182,6 @@ int lp_compact(void* stream, const uint8_t* mask, int64_t B, int64_t N, const vo
   compact_write_kernel<<<nblocks, 256, 0, st>>>(mask, slots, block_offsets, idx, pos);
   LP_LAUNCH_CHECK("compact_write_kernel");
   if (hidden != nullptr) {
-    DeviceInfo* di = nullptr;
-    int rc = current_device_info(&di);
-    if (rc) return rc;
     const int64_t warps = std::min<int64_t>(slots, (int64_t)di->sms * 32);
     compact_gather_kernel<<<(unsigned)cdiv(warps * 32, 256), 256, 0, st>>>(
         idx, count, N, reinterpret_cast<const __nv_bfloat16*>(hidden), hidden_bstride, hidden_rstride, row_offset, d,
@@ -1161,6 +1201,8 @@ int lp_scatter_rows(void* stream, const void* src, int64_t src_stride, const int
   if (rows_per_group <= 0) return fail(LP_EINVAL, "rows_per_group must be positive");
   if (slots == 0) return LP_OK;
   if (src == nullptr || pos == nullptr || out == nullptr) return fail(LP_EINVAL, "null src / pos / out");
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device_info(&di)) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (out_elem_bytes != elem_bytes) {
     if (width % 8 != 0 || src_stride % 4 != 0 || out_stride % 8 != 0 || group_stride % 8 != 0 ||
@@ -1201,6 +1243,8 @@ int lp_peer_barrier(void* stream, const unsigned long long* signal_pads, int ran
   if (signal_pads == nullptr) return fail(LP_EINVAL, "null signal_pads");
   if (world < 1 || world > 1024 || rank < 0 || rank >= world) return fail(LP_EINVAL, "bad rank %d / world %d", rank, world);
   if (channel < 0 || timeout_ms <= 0) return fail(LP_EINVAL, "bad channel %d or timeout %d ms", channel, timeout_ms);
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device_info(&di)) return rc;  // device set-up (host-visible error slot)
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int threads = (world + 31) / 32 * 32;
   ProfScope prof(st, "peer_barrier");

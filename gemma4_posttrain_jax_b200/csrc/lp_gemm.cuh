@@ -113,6 +113,7 @@ struct EpiParams {
   // (multimem.red); rank r then reduces its share of each block's rows (ld_reduce over all
   // copies through the NVSwitch, f32 accumulation) and stores the sum to all copies.
   __nv_bfloat16* sum_mc;        // multicast address of the output (row 0 of this launch)
+  __nv_bfloat16* sum_local;     // this rank's address of the same rows (NaN-filled on a timeout)
   long long sum_ld;             // output row stride (elements, multiple of 8)
   unsigned* cnt_local;          // this rank's copy of the per-128-row-block tile counters
   unsigned* cnt_mc;             // their multicast address
@@ -851,14 +852,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // share of its rows over all ranks' copies (ld_reduce through the NVSwitch) and store
         // the sum to every copy. The pair's CTAs split the share.
         const int b = un.red_block;
-        bool ready = true;
-        if (lane == 0)
-          ready = wait_counter_bounded(E.cnt_local + (size_t)b * (C::BM / 128), E.cnt_target, abort_flag,
-                                       E.peer_limit_ns);
-        if (!__shfl_sync(0xffffffffu, (int)ready, 0)) {
-          ok = false;
-          break;
-        }
         const int lo = b * C::BM + (E.sum_rank * C::BM) / E.sum_world;
         const int hi = b * C::BM + ((E.sum_rank + 1) * C::BM) / E.sum_world;
         const int r0 = lo + ((hi - lo) * (int)rank) / CG;
@@ -866,6 +859,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int vpr = S.N >> 3;  // 16-byte vectors per row
         const int nv = r0 < r1 ? (r1 - r0) * vpr : 0;
         constexpr int NT = EPI_WARPS * 32;
+        bool ready = true;
+        if (lane == 0)
+          ready = wait_counter_bounded(E.cnt_local + (size_t)b * (C::BM / 128), E.cnt_target, abort_flag,
+                                       E.peer_limit_ns);
+        if (!__shfl_sync(0xffffffffu, (int)ready, 0)) {
+          // another rank's tiles never arrived: this share of the sum does not exist, so its
+          // rows in this rank's copy get bf16 NaN rather than this rank's partial alone
+          const uint4 nan8 = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+          for (int v = ew * 32 + lane; v < nv; v += NT)
+            *reinterpret_cast<uint4*>(E.sum_local + (size_t)(r0 + v / vpr) * E.sum_ld + (v % vpr) * 8) = nan8;
+          ok = false;
+          break;
+        }
         for (int v0 = ew * 32 + lane; v0 < nv; v0 += 4 * NT) {
           uint4 acc[4];
 #pragma unroll

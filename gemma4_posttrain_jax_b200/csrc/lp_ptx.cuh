@@ -27,6 +27,10 @@ enum : int {
 // Device-side error code of this library (first error wins); read and cleared by
 // lp_device_error(). The library is one translation unit, so this is its only definition.
 __device__ int g_lp_device_error = 0;
+// Host-visible copy of the same code: a slot of mapped, pinned host memory (null until the
+// host has set it up for this device). The host reads it with lp_device_error_poll() at no
+// cost, with no CUDA call, once the kernels it cares about have completed.
+__device__ int* g_lp_host_error = nullptr;
 
 namespace lpk {
 
@@ -44,7 +48,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-__device__ __forceinline__ void record_device_error(int code) { atomicCAS(&g_lp_device_error, 0, code); }
+__device__ __forceinline__ void record_device_error(int code) {
+  if (atomicCAS(&g_lp_device_error, 0, code) == 0) {
+    int* h = g_lp_host_error;
+    if (h != nullptr) {
+      *reinterpret_cast<volatile int*>(h) = code;
+      __threadfence_system();
+    }
+  }
+}
 
 // ----------------------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -107,7 +107,8 @@ __device__ __forceinline__ float3 shard_triple(const float2* __restrict__ part, 
 //      (epoch * world: all ranks have stored), then merges the `world` triples of its rows
 //      exactly as combine_kernel does: logp = tgt - m - log s, norm = (m, s).
 // All blocks of the grid must be resident at once (the host keeps the grid at or below the
-// SM count), since a block only waits after its own stores.
+// SM count), since a block only waits after its own stores. A block whose wait runs out
+// records DEV_TIMEOUT_PEER and writes NaN to its rows of logp / norm.
 __global__ void fwd_finalize_mesh_kernel(const float2* __restrict__ part, int n_groups, int T,
                                          const float* __restrict__ tgt_ws, const int32_t* __restrict__ y,
                                          long long v_off, long long Vs, float4* xch_mc, const float4* xch_local,
@@ -149,7 +150,18 @@ __global__ void fwd_finalize_mesh_kernel(const float2* __restrict__ part, int n_
     s_go = go;
   }
   __syncthreads();
-  if (!s_go) return;
+  if (!s_go) {
+    // another rank never arrived: the merged values do not exist, so this block's rows
+    // get NaN instead of whatever the caller's buffers held
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += stride) {
+      if (logp != nullptr) logp[t] = __int_as_float(0x7fc00000);
+      if (norm != nullptr) {
+        norm[t] = __int_as_float(0x7fc00000);
+        norm[(size_t)T + t] = __int_as_float(0x7fc00000);
+      }
+    }
+    return;
+  }
   for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += stride) {
     float m = -INFINITY;
     for (int p = 0; p < world; ++p) m = fmaxf(m, __ldcg(&xch_local[(size_t)p * ld + t]).x);

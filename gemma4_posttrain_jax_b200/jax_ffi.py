@@ -110,7 +110,9 @@ def _local_logps(cap, sharded, token_chunk):
         w, h, y, norm = res
         dh, dw = _bwd_call(w, h, y, norm, g.astype(jnp.float32), cap, token_chunk)
         if sharded:
-            dh = lax.psum(dh.astype(jnp.float32), "d").astype(h.dtype)
+            # the bf16 partials are summed in bf16, as the reference's psum of the bf16 hidden
+            # cotangent (losses.py:253-259 transposed) and the torch binding's default do
+            dh = lax.psum(dh.astype(h.dtype), "d")
         return dw.astype(w.dtype), dh, None
 
     f.defvjp(fwd, bwd)

@@ -15,10 +15,11 @@ There is no fallback: other backends raise, CPU tensors raise, a missing library
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
-from . import ops
+from . import _lib, ops
 from .phase_timer import phase
 from .sharding import (
     VocabMesh,
@@ -26,6 +27,7 @@ from .sharding import (
     all_reduce_sum,
     dh_sum_buffer,
     peer_timeout_ms,
+    poison,
     stats_exchange,
     vocab_offset,
 )
@@ -35,6 +37,28 @@ from .sharding import (
 # or dW) when at least this fraction of the rows are zero; the reference's Pallas backward
 # skips all-zero 256-row blocks the same way (pallas/lm_head_logprob_tpuv4.py:185-193).
 _SKIP_ZERO_GRAD_MIN_FRACTION = 0.01
+
+
+def _check_device(device: torch.device, where: str) -> None:
+    """Raise if a kernel that has completed on ``device`` recorded a device-side error. Costs
+    a host load, no CUDA call: used right after the host has waited for the stream anyway."""
+    _lib.raise_on_device_error(device.index if device.index is not None else torch.cuda.current_device(), where)
+
+
+def _check_mesh_call(device: torch.device, mesh: VocabMesh, where: str) -> None:
+    """Wait for the current stream and raise if one of its kernels gave up waiting for another
+    rank (its outputs hold NaN where a result was missing). The mesh's multicast buffers are
+    then out of step between ranks, so they are marked unusable."""
+    torch.cuda.current_stream(device).synchronize()
+    try:
+        _check_device(device, where)
+    except _lib.DeviceTimeoutError:
+        poison(mesh, device)
+        raise
+
+
+def _debug_checks() -> bool:
+    return os.environ.get("LP_B200_DEBUG", "0") not in ("", "0")
 
 
 def _nonzero_grad_rows(g: torch.Tensor):
@@ -48,6 +72,7 @@ def _nonzero_grad_rows(g: torch.Tensor):
     mask = (g != 0).view(1, n)
     _, _, idx, pos, count = ops.compact(mask)
     m = int(count.item())
+    _check_device(g.device, "backward")  # the forward and everything before it have completed
     if n - m < _SKIP_ZERO_GRAD_MIN_FRACTION * n:
         return None
     return idx[:m], pos, m
@@ -97,6 +122,7 @@ def _backward_rows(embed, H, y, softcap, norm, g, *, mesh, vocab_offset, need_dh
                                     token_chunk=token_chunk, dh_mesh_sum=buf)
         with phase("dh_peer_barrier"):
             ops.peer_barrier(buf, timeout)  # every rank's share of the sum has landed everywhere
+        _check_mesh_call(H.device, mesh, "lp_bwd_sum (dH summed over the mesh)")
         return dH, dW, pos, True
     dH, dW = ops.shard_backward(embed, Hz, yz, softcap, nz, gz, vocab_offset=vocab_offset, need_dh=need_dh,
                                 need_dw=need_dw, dh_dtype=dh_dtype, dw_dtype=dw_dtype, token_chunk=token_chunk)
@@ -112,7 +138,9 @@ def _mesh_forward(embed, H, y, softcap, mesh, off):
     (``lp_fwd_sum``) where the mesh has a multicast buffer, else NCCL all-gather + combine."""
     xch = stats_exchange(mesh, H.shape[0], H.device)
     if xch is not None:
-        return ops.shard_forward_sum(embed, H, y, softcap, xch, vocab_offset=off, timeout_ms=peer_timeout_ms())
+        out = ops.shard_forward_sum(embed, H, y, softcap, xch, vocab_offset=off, timeout_ms=peer_timeout_ms())
+        _check_mesh_call(H.device, mesh, "lp_fwd_sum (triples exchanged over the mesh)")
+        return out
     stats, _ = ops.shard_forward(embed, H, y, softcap, vocab_offset=off, want_logp=False)
     with phase("stats_all_gather"):
         gathered = all_gather_stats(stats, mesh)
@@ -254,13 +282,21 @@ class _CompletionLogps(torch.autograd.Function):
                 dh_reduce_f32=False, skip_zero_grad=True):
         B, N = completion_mask.shape
         Hc, yc, idx, pos, count = ops.compact(completion_mask, hidden, completion_ids, row_offset=prompt_width - 1)
-        n = int(count.item()) if num_valid is None else int(num_valid)
+        if num_valid is None:
+            n = int(count.item())
+            _check_device(hidden.device, "completion_logps")
+        else:
+            n = int(num_valid)
+            if _debug_checks():
+                _check_num_valid(count, n)
         Hn, yn = Hc[:n], yc[:n]
         P = mesh.size if mesh is not None else 1
         off = vocab_offset(embed.shape[0], mesh) if P > 1 else 0
         if n > 0:
             if P > 1:
                 logp_c, norm = _mesh_forward(embed, Hn, yn, softcap, mesh, off)
+                if num_valid is not None and not _debug_checks():
+                    _check_num_valid(count, n)  # the mesh forward has waited for the stream: free
             else:
                 stats, logp_c = ops.shard_forward(embed, Hn, yn, softcap, want_logp=True)
                 norm = stats[:2]
@@ -310,6 +346,14 @@ class _CompletionLogps(torch.autograd.Function):
         return dW, dhidden, None, None, None, None, None, None, None, None, None
 
 
+def _check_num_valid(count: torch.Tensor, n: int) -> None:
+    """A caller's ``num_valid`` must be the mask's popcount: fewer would drop valid slots and
+    more would read compacted rows that were never written."""
+    c = int(count.item())
+    if c != n:
+        raise ValueError(f"num_valid={n} but completion_mask has {c} valid slots")
+
+
 def completion_logps(
     embed_tokens: torch.Tensor,
     hidden: torch.Tensor,
@@ -330,7 +374,9 @@ def completion_logps(
     by position ``prompt_width + j - 1``. Only ``completion_mask`` slots are computed
     (compaction); invalid slots return 0, as ``where(completion_mask, logps, 0)`` does.
     ``num_valid`` (the mask's popcount, when the caller knows it on the host) avoids one
-    device-to-host read. ``dh_reduce_f32``, ``skip_zero_grad``: see ``per_token_logps``.
+    device-to-host read; it is checked against the device count wherever the call waits for
+    the GPU anyway (vocabulary-sharded calls) and always with ``LP_B200_DEBUG=1``.
+    ``dh_reduce_f32``, ``skip_zero_grad``: see ``per_token_logps``.
     """
     if hidden.ndim != 3 or completion_ids.ndim != 2 or completion_mask.shape != completion_ids.shape:
         raise ValueError("hidden must be [B, S, d] and completion ids / mask [B, N]")

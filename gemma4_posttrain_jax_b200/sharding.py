@@ -150,8 +150,63 @@ def dh_reduce_mode(mesh: VocabMesh | None) -> str:
 
 
 def peer_timeout_ms() -> int:
-    """Bound of every device-side wait of lp_peer_barrier (``LP_B200_PEER_TIMEOUT_MS``)."""
-    return max(1, int(os.environ.get("LP_B200_PEER_TIMEOUT_MS", "60000")))
+    """Bound of every device-side wait for another rank (``LP_B200_PEER_TIMEOUT_MS``).
+
+    The waits cover the skew between ranks reaching the same call: another rank's forward
+    or dH GEMM (about 0.1 s for the config-2 batch on one GPU) plus that rank's host-side
+    stalls. The default of 10 s is about 30 times the longest of those GEMMs; a rank that
+    has not arrived by then is treated as lost and the call raises."""
+    return max(1, int(os.environ.get("LP_B200_PEER_TIMEOUT_MS", "10000")))
+
+
+class MulticastUnavailable(RuntimeError):
+    """The mesh cannot use NVLS multicast buffers (decided by every rank together)."""
+
+
+def _all_ranks_agree(mesh: VocabMesh, ok: bool, device: torch.device) -> bool:
+    """True only where ``ok`` holds on every rank of the mesh. One all-reduce, so every rank
+    takes the same branch: a rank whose allocation failed never leaves its peers waiting in
+    a rendezvous or in a kernel that expects it."""
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=mesh.group)
+    return bool(int(flag.item()) == 1)
+
+
+def _symmetric_alloc(mesh: VocabMesh, nbytes: int, device: torch.device):
+    """(storage, rendezvous handle) of ``nbytes`` of symmetric memory with a multicast
+    mapping on every rank, or MulticastUnavailable on every rank alike."""
+    group = mesh.group if mesh.group is not None else dist.group.WORLD
+    storage = None
+    try:
+        import torch.distributed._symmetric_memory as symm_mem  # noqa: PLC0415 - CUDA + NCCL only
+
+        storage = symm_mem.empty((nbytes,), dtype=torch.uint8, device=device)
+    except (RuntimeError, ImportError):  # includes torch.OutOfMemoryError
+        storage = None
+    if not _all_ranks_agree(mesh, storage is not None, device):
+        raise MulticastUnavailable("symmetric memory could not be allocated on every rank")
+    handle = symm_mem.rendezvous(storage, group)
+    if not _all_ranks_agree(mesh, int(handle.multicast_ptr) != 0, device):
+        raise MulticastUnavailable("symmetric memory has no multicast mapping on every rank")
+    return storage, handle
+
+
+# Meshes whose multicast buffers a device-side peer timeout left out of step (their exchange
+# counters no longer agree between ranks): later calls on them raise instead of waiting.
+_POISONED: set[tuple] = set()
+
+
+def poison(mesh: VocabMesh, device: torch.device) -> None:
+    """Mark the mesh's multicast buffers on ``device`` unusable after a peer timeout."""
+    _POISONED.add((id(mesh.group), device.index))
+
+
+def _check_not_poisoned(gkey: tuple) -> None:
+    if gkey in _POISONED:
+        raise RuntimeError(
+            "an earlier call on this vocabulary mesh gave up waiting for another rank, which left its NVLink "
+            "exchange buffers out of step; create a new process group (and mesh) before calling again"
+        )
 
 
 class DhSumBuffer:
@@ -162,25 +217,20 @@ class DhSumBuffer:
     partials (``losses.py:253-259`` transposed) done while the GEMM runs."""
 
     def __init__(self, mesh: VocabMesh, rows: int, d: int, device: torch.device):
-        import torch.distributed._symmetric_memory as symm_mem  # noqa: PLC0415 - CUDA + NCCL only
-
         from . import _lib  # noqa: PLC0415
 
-        group = mesh.group if mesh.group is not None else dist.group.WORLD
         self.rows, self.d, self.device = int(rows), int(d), device
         self.n_counters = int(_lib.load().lp_bwd_sum_counters(self.rows))
         dh_bytes = -(-self.rows * self.d * 2 // 4096) * 4096
         total = dh_bytes + -(-self.n_counters * 4 // 4096) * 4096
-        self.storage = symm_mem.empty((total,), dtype=torch.uint8, device=device)
+        self.storage, self.handle = _symmetric_alloc(mesh, total, device)
         self.dh = self.storage[: self.rows * self.d * 2].view(torch.bfloat16).view(self.rows, self.d)
         self.counters = self.storage[dh_bytes : dh_bytes + self.n_counters * 4].view(torch.int32)
         self.counters.zero_()
-        self.handle = symm_mem.rendezvous(self.storage, group)
         mc = int(self.handle.multicast_ptr)
-        if mc == 0:
-            raise RuntimeError("symmetric memory has no multicast mapping on this system")
+        # the same on every rank (same world size and signal pad size)
         if (_BARRIER_CHANNEL + 1) * self.handle.world_size * 4 > self.handle.signal_pad_size:
-            raise RuntimeError("signal pad too small for the barrier channel")
+            raise MulticastUnavailable("signal pad too small for the barrier channel")
         self.dh_mc = mc
         self.counters_mc = mc + dh_bytes
         self.pads_dev = int(self.handle.signal_pad_ptrs_dev)
@@ -196,9 +246,10 @@ def dh_sum_buffer(mesh: VocabMesh, rows: int, d: int, device: torch.device) -> D
     """The mesh's multicast dH buffer with room for ``rows`` x ``d`` (collective when it has to
     grow: every rank holds the same row count because the upstream gradient is replicated),
     or None where the multicast path is off or the system has no NVLS multicast."""
+    gkey = (id(mesh.group), device.index)
+    _check_not_poisoned(gkey)
     if dh_reduce_mode(mesh) != "multimem":
         return None
-    gkey = (id(mesh.group), device.index)
     if gkey in _MULTICAST_UNAVAILABLE:
         return None
     key = (*gkey, int(d))
@@ -211,7 +262,7 @@ def dh_sum_buffer(mesh: VocabMesh, rows: int, d: int, device: torch.device) -> D
         buf = None
         try:
             buf = DhSumBuffer(mesh, grow, d, device)
-        except (RuntimeError, ImportError):
+        except MulticastUnavailable:
             _MULTICAST_UNAVAILABLE.add(gkey)
             return None
         _DH_BUFFERS[key] = buf
@@ -242,21 +293,17 @@ class StatsExchange:
     ``losses.py:219,243-245`` as one NVLink exchange inside the forward)."""
 
     def __init__(self, mesh: VocabMesh, rows: int, device: torch.device):
-        import torch.distributed._symmetric_memory as symm_mem  # noqa: PLC0415 - CUDA + NCCL only
-
-        group = mesh.group if mesh.group is not None else dist.group.WORLD
         self.rows, self.device = int(rows), device
         world = mesh.size
         slot_bytes = -(-world * self.rows * 16 // 4096) * 4096
         self.slot_bytes = slot_bytes
         total = 2 * slot_bytes + 4096  # two exchange buffers + counters (128 B apart) + arrivals
-        self.storage = symm_mem.empty((total,), dtype=torch.uint8, device=device)
+        self.storage, self.handle = _symmetric_alloc(mesh, total, device)
         self.storage[2 * slot_bytes :].zero_()
-        torch.cuda.synchronize(device)  # counters are zero on every rank before any rank signals
-        self.handle = symm_mem.rendezvous(self.storage, group)
+        torch.cuda.synchronize(device)
+        # counters are zero on every rank before any rank signals
+        _all_ranks_agree(mesh, True, device)
         mc = int(self.handle.multicast_ptr)
-        if mc == 0:
-            raise RuntimeError("symmetric memory has no multicast mapping on this system")
         self.base, self.base_mc = int(self.storage.data_ptr()), mc
         self.rank, self.world = int(self.handle.rank), int(self.handle.world_size)
         self.calls = 0
@@ -276,9 +323,10 @@ def stats_exchange(mesh: VocabMesh, rows: int, device: torch.device) -> StatsExc
     """The mesh's multicast stats exchange with room for ``rows`` tokens (collective when it
     has to grow: every rank holds the same token count because hidden states and targets
     are replicated), or None where the multicast path is off or unavailable."""
+    gkey = (id(mesh.group), device.index)
+    _check_not_poisoned(gkey)
     if stats_exchange_mode(mesh) != "multimem":
         return None
-    gkey = (id(mesh.group), device.index)
     if gkey in _MULTICAST_UNAVAILABLE:
         return None
     buf = _STATS_EXCHANGES.get(gkey)
@@ -289,7 +337,7 @@ def stats_exchange(mesh: VocabMesh, rows: int, device: torch.device) -> StatsExc
         _STATS_EXCHANGES.pop(gkey, None)
         try:
             buf = StatsExchange(mesh, grow, device)
-        except (RuntimeError, ImportError):
+        except MulticastUnavailable:
             _MULTICAST_UNAVAILABLE.add(gkey)
             return None
         _STATS_EXCHANGES[gkey] = buf

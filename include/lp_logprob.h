@@ -95,8 +95,16 @@ LP_API int lp_profile_enable(int on);
 LP_API int lp_profile_read(int max_tags, char* names, double* total_ms, long long* launches, int* n_tags);
 
 /* Reads and clears the device-side error code recorded by kernels on `device`
- * (0 = none; 1..4 = a bounded wait gave up). Synchronises that device. */
+ * (0 = none; 1..4 = a bounded wait inside a GEMM gave up; 5 = a wait for another rank of a
+ * vocabulary mesh gave up). Synchronises that device. */
 LP_API int lp_device_error(int device, int* code);
+
+/* The same code without any CUDA call or synchronisation: kernels also write it to mapped
+ * host memory, so a caller that has already waited for its stream (for instance to read a
+ * count back) can check the kernels it waited for at no cost. Returns 0 while nothing has
+ * been recorded on `device` since the last lp_device_error(device, ...) (which clears it),
+ * and 0 before the library has run anything on that device. */
+LP_API int lp_device_error_poll(int device);
 
 /* Scratch bytes lp_fwd needs for T tokens against a shard of Vs rows. */
 LP_API size_t lp_fwd_workspace_bytes(int64_t T, int64_t Vs);
@@ -114,8 +122,9 @@ LP_API size_t lp_fwd_workspace_bytes(int64_t T, int64_t Vs);
 LP_API int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs, int64_t v_off,
            const int32_t* y, float softcap, float* stats, float* logp, void* workspace, size_t workspace_bytes);
 
-/* Size of the fixed device scratch lp_fwd_noalloc uses (held by every GPU that loads the
- * library, from its first lp_fwd_noalloc call until the process exits). */
+/* Size of the fixed device scratch lp_fwd_noalloc uses. The library's device code is one
+ * module, so every GPU on which the library has run any kernel holds this array until the
+ * process exits, whether or not it ever calls lp_fwd_noalloc. */
 #define LP_NOALLOC_SCRATCH_BYTES (8u << 20)
 
 /*
@@ -132,8 +141,14 @@ LP_API int lp_fwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh
  *     or different host threads) race and corrupt each other's results: serialise them.
  *     The array keeps the last call's contents; every scratch value a call reads is
  *     written earlier in that same call, so nothing needs clearing between calls.
- *   - Token counts whose scratch exceeds the limit (about 690k tokens; fewer when the
- *     tile plan keeps several vocabulary groups) return LP_EINVAL with a message.
+ *   - The scratch holds 16 bytes per token for each vocabulary group of the tile plan
+ *     (a running max and sum for each half of a group's columns) plus a 4-byte target
+ *     logit per token. Where lp_fwd's plan would need more, the groups are widened (fewer
+ *     groups of more 256-row vocabulary tiles; the results are the same); with a single
+ *     group the limit is 419,424 tokens (8 MiB / 20 B, less 256-byte alignment). More tokens
+ *     return LP_EINVAL.
+ *     Wider groups make fewer, longer work units (ceil(T / 128) x groups): above about
+ *     233k tokens there is one group, so each unit streams the whole shard for 128 rows.
  */
 LP_API int lp_fwd_noalloc(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, const void* W, int64_t Vs,
                           int64_t v_off, const int32_t* y, float softcap, float* stats, float* logp);

@@ -239,8 +239,10 @@ def logps_grads_f64(
     softcap: float | None,
     *,
     vocab_block: int = 16384,
+    want_dw: bool = True,
 ):
-    """Analytic VJP of the logprob path in float64: returns ``(logp, dW, dH)``.
+    """Analytic VJP of the logprob path in float64: returns ``(logp, dW, dH)`` (dW is None
+    with ``want_dw=False``, which checks sampled rows of a large vocabulary cheaply).
 
     With x = h . w_v, z = softcap(x), p = softmax(z):
       d logp_t / d z_tv = 1[v = y_t] - p_tv          (the max shift has no gradient,
@@ -272,7 +274,7 @@ def logps_grads_f64(
     logp = zt - lse
     # pass 2: gradients
     dH = np.zeros_like(h)
-    dW = np.zeros_like(e)
+    dW = np.zeros_like(e) if want_dw else None
     rows = np.arange(T)
     for v0 in range(0, V, vocab_block):
         x = h @ e[v0 : v0 + vocab_block].T
@@ -288,7 +290,8 @@ def logps_grads_f64(
         dz[rows[inblk], t[inblk] - v0] += 1.0
         dx = gg[:, None] * dz * chain
         dH += dx @ e[v0 : v0 + vocab_block]
-        dW[v0 : v0 + vocab_block] += dx.T @ h
+        if want_dw:
+            dW[v0 : v0 + vocab_block] += dx.T @ h
     return logp.reshape(targets.shape), dW, dH.reshape(hidden.shape)
 
 

@@ -2,7 +2,12 @@
 
 Every rank draws the same seeded inputs, keeps its vocabulary row block, and runs the
 public API (per_token_logps and completion_logps, forward + backward) over an NCCL mesh.
-Rank 0 gathers the dW shards and checks logps, dH and dW against the CPU oracle.
+Rank 0 gathers the dW shards and checks logps, dH and dW against the CPU oracle. A
+config-2-shaped case (32768 vocabulary rows per rank, d = 2048, 12288 tokens, zero-gradient
+rows) runs the production plan of the fused NVLink forward exchange and in-GEMM dH sum; it
+is checked in full against a float32 PyTorch computation on the GPUs (bench.py's parity
+check: every logp, 256 dH rows, 256 dW rows per shard) and on sampled rows against the
+oracle.
 """
 
 from __future__ import annotations
@@ -77,9 +82,59 @@ def check_per_token(mesh, dev, rank, world, mode, V, T, d, seed, stats_mode="mul
     return ok
 
 
+def check_config2_shape(mesh, dev, rank, world, seed, T=12288, d=2048, Vs=32768) -> bool:
+    """The production plan (Vs = 32768 per rank as in config 2 at 8 GPUs, d = 2048) of the
+    NVLink forward exchange and the in-GEMM dH sum, checked in full and against the oracle."""
+    from bench import parity_check
+
+    os.environ["LP_B200_DH_REDUCE"] = "multimem"
+    os.environ["LP_B200_STATS_EXCHANGE"] = "multimem"
+    V = Vs * world
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    W_full = (torch.randn((V, d), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    H = torch.randn((T, d), generator=gen, device=dev).to(torch.bfloat16)
+    y = torch.randint(0, V, (T,), generator=gen, device=dev, dtype=torch.int32)
+    y[:4] = torch.tensor([0, Vs - 1, Vs, V - 1], dtype=torch.int32, device=dev)
+    g = torch.randn((T,), generator=gen, device=dev) * (torch.rand((T,), generator=gen, device=dev) < 0.9)
+    g[256:768] = 0.0  # two whole zero-gradient row blocks
+    W = W_full[rank * Vs : (rank + 1) * Vs].clone().requires_grad_(True)
+    w_host = W_full.float().cpu().numpy() if rank == 0 else None
+    ok = True
+    for rep in range(2):  # the second call reuses the multicast buffers
+        W.grad = None
+        Hq = H.clone().requires_grad_(True)
+        lp = per_token_logps(W, Hq, y, softcap=30.0, mesh=mesh)
+        lp.backward(g)
+        torch.cuda.synchronize()
+        par = parity_check(W, H, y, g, lp.detach(), W.grad, Hq.grad, softcap=30.0, rank=rank, world=world, dev=dev)
+        if rank == 0:
+            gen_r = np.random.default_rng(seed + rep)
+            rows = np.sort(gen_r.choice(np.nonzero(g.cpu().numpy())[0], size=16, replace=False))
+            h = H.float().cpu().numpy()[rows]
+            lp_o, _, dh_o = orc.logps_grads_f64(w_host, h, y.cpu().numpy()[rows], g.cpu().numpy()[rows], 30.0,
+                                                want_dw=False)
+            e_lp_o = float(np.abs(lp.detach().cpu().numpy()[rows] - lp_o).max())
+            e_dh_o = rel_l2(Hq.grad.float().cpu().numpy()[rows], dh_o)
+            print(f"world={world} config-2 shape (Vs={Vs}, d={d}, T={T}) call {rep + 1}: dH sum="
+                  f"{sharding.dh_reduce_mode(mesh)} stats={sharding.stats_exchange_mode(mesh)}; float32 check: "
+                  f"logp max abs {par['logp_max_abs']:.2e} (all {T} tokens), dH rel-L2 {par['dh_rel_l2']:.2e}, "
+                  f"dW rel-L2 {par['dw_rel_l2']:.2e}, zero rows zero {par['zero_grad_rows_zero']}; oracle on 16 "
+                  f"rows: logp {e_lp_o:.2e}, dH rel-L2 {e_dh_o:.2e}", flush=True)
+            ok = ok and par["ok"] and e_lp_o <= 2e-3 and e_dh_o <= 1e-2
+        del lp, Hq
+        # the other ranks wait here (host side) while rank 0 runs the CPU oracle, not inside
+        # the next call's bounded device-side wait for rank 0
+        dist.barrier(device_ids=[dev.index])
+    return ok
+
+
 def main() -> int:
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     os.environ.setdefault("LP_B200_PEER_TIMEOUT_MS", "10000")
+    if rank == 0:  # the CPU oracle may use every core (torchrun gives each rank one thread)
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=len(os.sched_getaffinity(0)), user_api="blas")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
@@ -92,6 +147,7 @@ def main() -> int:
     # exchange buffer grows (a new multicast buffer) for the larger token count
     ok = check_per_token(mesh, dev, rank, world, "multimem", 8192 * world, 2100, 392, 7) and ok
     ok = check_per_token(mesh, dev, rank, world, "multimem", 8192 * world, 2100, 392, 7, stats_mode="nccl") and ok
+    ok = check_config2_shape(mesh, dev, rank, world, seed=11) and ok
     os.environ["LP_B200_DH_REDUCE"] = "multimem"
     os.environ["LP_B200_STATS_EXCHANGE"] = "multimem"
     rng = np.random.default_rng(20260926)

@@ -148,8 +148,10 @@ def test_mesh_forward_routes_to_the_nvlink_exchange_or_the_all_gather(monkeypatc
     monkeypatch.setattr(losses, "all_gather_stats", gather)
     monkeypatch.setenv("LP_B200_PEER_TIMEOUT_MS", "1234")
     monkeypatch.setattr(losses, "stats_exchange", lambda m, rows, dev: "xch")
+    # after the exchange the call waits for its stream and raises on a recorded peer timeout
+    monkeypatch.setattr(losses, "_check_mesh_call", lambda dev, m, where: calls.append(("check", where.split()[0])))
     assert losses._mesh_forward(W, H, y, 30.0, mesh, 6) == (logp, norm)
-    assert calls == [("lp_fwd_sum", "xch", 6, 1234)]
+    assert calls == [("lp_fwd_sum", "xch", 6, 1234), ("check", "lp_fwd_sum")]
     calls.clear()
     monkeypatch.setattr(losses, "stats_exchange", lambda m, rows, dev: None)
     assert losses._mesh_forward(W, H, y, 30.0, mesh, 6) == (logp, norm)
@@ -158,7 +160,8 @@ def test_mesh_forward_routes_to_the_nvlink_exchange_or_the_all_gather(monkeypatc
 
 def test_mesh_backward_routes_the_dh_sum(monkeypatch):
     """The backward of a vocabulary mesh: with a multicast dH buffer, zeroed counters, a peer
-    barrier, the fused lp_bwd_sum backward and a second barrier (dH shared with the buffer);
+    barrier, the fused lp_bwd_sum backward, a second barrier (dH shared with the buffer) and
+    the host-side check for a peer timeout;
     without one, the plain backward and an all-reduce of dH. Device calls are stubbed; only
     the routing and its order are checked."""
     import torch
@@ -185,6 +188,7 @@ def test_mesh_backward_routes_the_dh_sum(monkeypatch):
     monkeypatch.setattr(losses.ops, "bwd_sum_counters", lambda rows: 4)
     monkeypatch.setattr(losses.ops, "peer_barrier", lambda buf, t: calls.append(("barrier", t)))
     monkeypatch.setattr(losses, "all_reduce_sum", lambda t, m: calls.append(("all_reduce", t.dtype, tuple(t.shape))) or t)
+    monkeypatch.setattr(losses, "_check_mesh_call", lambda dev, m, where: calls.append(("check", where.split()[0])))
     monkeypatch.setenv("LP_B200_PEER_TIMEOUT_MS", "777")
     kw = dict(mesh=FakeMesh(), vocab_offset=10, need_dh=True, need_dw=True, dh_dtype=torch.bfloat16,
               dw_dtype=torch.float32, token_chunk=None, skip_zero_grad=False)
@@ -193,7 +197,8 @@ def test_mesh_backward_routes_the_dh_sum(monkeypatch):
     monkeypatch.setattr(losses, "dh_sum_buffer", lambda m, rows, dd, dev: buf)
     dH, dW, pos, shared = losses._backward_rows(W, H, y, 30.0, norm, g, **kw)
     assert shared and pos is None
-    assert calls == [("barrier", 777), ("lp_bwd_sum", 10, torch.bfloat16), ("barrier", 777)]
+    # ... and the host waits for the stream, raising on a recorded peer timeout
+    assert calls == [("barrier", 777), ("lp_bwd_sum", 10, torch.bfloat16), ("barrier", 777), ("check", "lp_bwd_sum")]
     assert buf.counters[:4].eq(0).all() and buf.counters[4:].eq(7).all()  # the used counters are zeroed
 
     calls.clear()

@@ -68,3 +68,40 @@ def test_context_usable_after_a_timed_out_wait(cuda_device):
     torch.cuda.synchronize()
     assert _lib.device_error(0) == 0
     assert np.abs(lp.cpu().numpy() - orc.dense_logps(w, h, y, 30.0)).max() <= 2e-3
+
+
+def test_recorded_timeout_raises_at_the_next_host_sync(cuda_device):
+    """A device error is not silent in the product path: the first place where the library
+    waits for the GPU (here the backward's row count, and completion_logps' valid-slot
+    count) raises, naming the code, until the code is read and cleared."""
+    from gemma4_posttrain_jax_b200 import _lib, completion_logps, per_token_logps
+    from gemma4_posttrain_jax_b200.ops import _stream
+
+    lib = _lib.load()
+    pads = [torch.zeros(64, dtype=torch.int32, device=cuda_device) for _ in range(2)]
+    ptrs = torch.tensor([p.data_ptr() for p in pads], dtype=torch.int64, device=cuda_device)
+    lib.lp_peer_barrier(_stream(cuda_device), ctypes.c_void_p(ptrs.data_ptr()), 0, 2, 1, 100)
+    torch.cuda.synchronize()
+    assert _lib.device_error_poll(0) == DEV_TIMEOUT_PEER  # visible on the host without a CUDA call
+
+    rng = np.random.default_rng(4)
+    w = orc.bf16_round(rng.normal(size=(300, 64)) * 0.5)
+    h = orc.bf16_round(rng.normal(size=(40, 64)))
+    y = rng.integers(0, 300, size=40).astype(np.int32)
+    g = rng.normal(size=40).astype(np.float32)
+    g[:10] = 0.0
+    W = torch.from_numpy(w).to(cuda_device).to(torch.bfloat16).requires_grad_(True)
+    H = torch.from_numpy(h).to(cuda_device).to(torch.bfloat16).requires_grad_(True)
+    lp = per_token_logps(W, H, torch.from_numpy(y).to(cuda_device), softcap=30.0)
+    with pytest.raises(_lib.DeviceTimeoutError, match="DEV_TIMEOUT_PEER"):
+        lp.backward(torch.from_numpy(g).to(cuda_device))
+    mask = torch.ones((2, 20), dtype=torch.bool, device=cuda_device)
+    with pytest.raises(_lib.DeviceTimeoutError, match="DEV_TIMEOUT_PEER"):
+        completion_logps(W, H.detach().view(2, 20, 64), torch.from_numpy(y).to(cuda_device).view(2, 20), mask,
+                         prompt_width=1, softcap=30.0)
+    assert _lib.device_error(0) == DEV_TIMEOUT_PEER  # read and cleared (both copies)
+    assert _lib.device_error_poll(0) == 0
+    lp = per_token_logps(W, H, torch.from_numpy(y).to(cuda_device), softcap=30.0)
+    lp.backward(torch.from_numpy(g).to(cuda_device))
+    torch.cuda.synchronize()
+    assert np.abs(lp.detach().cpu().numpy() - orc.dense_logps(w, h, y, 30.0)).max() <= 2e-3

@@ -5,9 +5,11 @@ custom call that only receives its input and output buffers, a host loop that mu
 grow device memory after start-up); its scratch is a fixed array inside the library. This
 test calls it through the C ABI twice in a row, on the same inputs as the existing entry
 point, and checks both calls against lp_fwd with the tolerances of the other forward tests
-(per-token logp within 2e-3; statistics as in test_forward_stats_and_logps). It lives in
-its own file so pytest collects it last, and it must pass in a fresh process as well as
-after the other tests.
+(per-token logp within 2e-3; statistics as in test_forward_stats_and_logps), and a sample
+of rows against the CPU oracle. The largest case needs more scratch than lp_fwd's tile
+plan would use, so the entry point widens its vocabulary groups (fewer groups of more
+tiles) to fit. It lives in its own file so pytest collects it last, and it must pass in a
+fresh process as well as after the other tests.
 """
 
 from __future__ import annotations
@@ -48,9 +50,28 @@ def _noalloc(lib, dev, W, H, Y, softcap, v_off=0, want_logp=True):
     return stats, logp
 
 
+def _default_groups(T, V):
+    """Vocabulary groups of lp_fwd's plan (lp_capi.cu plan_fwd) and the scratch they need."""
+    tiles = -(-V // 256)
+    g = 1
+    while g < tiles and 2 * (-(-tiles // g)) * T * 8 > (128 << 20):
+        g *= 2
+    g = max(g, min(4, tiles))
+    groups = -(-tiles // g)
+    up = lambda x: -(-x // 256) * 256  # noqa: E731
+    return groups, up(2 * groups * T * 8) + up(4 * T)
+
+
+def test_widening_case_exceeds_the_default_plan():
+    # the last case below would need more than the fixed scratch with lp_fwd's groups
+    groups, need = _default_groups(60000, 70000)
+    assert groups == 69 and need > (8 << 20)
+
+
 @pytest.mark.parametrize(
     "T,V,d,scale,softcap,v_off",
-    [(513, 1036, 128, 1.5, 30.0, 0), (513, 1036, 128, 0.04, None, 0), (4099, 70000, 256, 0.3, 30.0, 12345)],
+    [(513, 1036, 128, 1.5, 30.0, 0), (513, 1036, 128, 0.04, None, 0), (4099, 70000, 256, 0.3, 30.0, 12345),
+     (60000, 70000, 64, 0.5, 30.0, 0)],
 )
 def test_noalloc_forward_matches_workspace_forward(cuda_device, T, V, d, scale, softcap, v_off):
     from gemma4_posttrain_jax_b200 import _lib, ops
@@ -73,6 +94,13 @@ def test_noalloc_forward_matches_workspace_forward(cuda_device, T, V, d, scale, 
         np.testing.assert_allclose(s[2], r[2], atol=2e-4, rtol=2e-5)
         if want_logp:
             assert np.abs(logp.cpu().numpy() - ref_logp.cpu().numpy()).max() <= LOGP_ATOL
+    if want_logp:
+        # a sample of rows against the CPU oracle (float64 dense log-softmax)
+        rows = np.random.default_rng(T).choice(T, size=min(T, 384), replace=False)
+        w = W.float().cpu().numpy()
+        h = H.float().cpu().numpy()[rows]
+        ref = orc.dense_logps(w, h, Y.cpu().numpy()[rows], softcap)
+        assert np.abs(logp.cpu().numpy()[rows] - ref).max() <= LOGP_ATOL
 
 
 def test_noalloc_forward_refuses_oversized_requests(cuda_device):
