@@ -90,6 +90,9 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true", help="skip the float32 check of one step's results")
+    p.add_argument("--vocab-per-gpu", type=int, default=0,
+                   help="tuning only: vocabulary rows per GPU (default V / N); e.g. 32768 on one GPU runs the "
+                        "per-GPU shard of an 8-GPU mesh without its collectives (the line's vocab says so)")
     return p.parse_args()
 
 
@@ -104,20 +107,20 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def make_batch(batch: int, seed: int = SEED):
+def make_batch(batch: int, seed: int = SEED, vocab: int = V):
     """Seeded synthetic GRPO batch (host numpy for masks / ids / advantages)."""
     rng = np.random.default_rng(seed)
     prompt_len = rng.integers(128, PROMPT + 1, size=batch)  # left-padded to 512: does not move the slice
     resp_len = rng.integers(64, RESP + 1, size=batch)
     mask = np.arange(RESP)[None, :] < resp_len[:, None]
-    ids = rng.integers(0, V, size=(batch, RESP)).astype(np.int32)
+    ids = rng.integers(0, vocab, size=(batch, RESP)).astype(np.int32)
     adv = rng.normal(size=(batch, 1)).astype(np.float32)
     keep = rng.random((batch, RESP)) < 0.9
     g = np.where(mask & keep, adv, 0.0).astype(np.float32)
     return prompt_len, resp_len, mask, ids, g
 
 
-def config_dict(batch, n_valid, world, softcap):
+def config_dict(batch, n_valid, world, softcap, vocab=V):
     return {
         "workload": "grpo_response_logprob_fwd_bwd (BASELINE config 2)",
         "global_batch": batch,
@@ -126,8 +129,8 @@ def config_dict(batch, n_valid, world, softcap):
         "response_width": RESP,
         "valid_tokens": int(n_valid),
         "hidden": D,
-        "vocab": V,
-        "vocab_per_gpu": V // world,
+        "vocab": vocab,
+        "vocab_per_gpu": vocab // world,
         "softcap": softcap if softcap > 0 else None,
         "parallelism": f"vocab{world}",
         "l2": "no flush: W shard + hidden exceed the 126 MB L2 (>= 0.8 GB each)",
@@ -480,15 +483,16 @@ class Workload:
 def grpo_workload(args, dev, rank, world, mesh, softcap, chunk):
     from gemma4_posttrain_jax_b200.losses import completion_logps
 
-    prompt_len, resp_len, mask_np, ids_np, g_np = make_batch(args.batch)
+    vs = args.vocab_per_gpu or V // world
+    vocab = vs * world
+    prompt_len, resp_len, mask_np, ids_np, g_np = make_batch(args.batch, vocab=vocab)
     n_valid = int(mask_np.sum())
     # rows the backward computes: valid tokens with nonzero dlogp (zero-gradient rows are
     # skipped by the library, as the reference's Pallas backward skips all-zero blocks)
     n_bwd = int((g_np[mask_np] != 0).sum())
-    vs = V // world
     # inputs: the same seeded draws on every rank; each rank keeps its W row block
     gen = torch.Generator(device=dev).manual_seed(SEED + 1)
-    W_full = (torch.randn((V, D), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    W_full = (torch.randn((vocab, D), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
     W = W_full[rank * vs : (rank + 1) * vs].clone().requires_grad_(True)
     del W_full
     gen_h = torch.Generator(device=dev).manual_seed(SEED + 2)
@@ -513,18 +517,20 @@ def grpo_workload(args, dev, rank, world, mesh, softcap, chunk):
     return Workload(
         W=W, inputs=[H, ids, mask, g], step=step, parity_view=parity_view, n_valid=n_valid, n_bwd=n_bwd, d=D, vs=vs,
         flops={"fwd_lse_gemm": 2.0 * n_valid * D * vs, "bwd_dz_gemm": bwd, "bwd_dh_gemm": bwd, "bwd_dw_gemm": bwd},
-        total_flops=2.0 * n_valid * D * V + 6.0 * n_bwd * D * V, dense_flops=8.0 * n_valid * D * V,
-        out_shape=(args.batch, RESP), metric=METRIC, config=config_dict(args.batch, n_valid, world, args.softcap),
-        traffic_ok=world == 1 and args.batch == B and args.softcap == SOFTCAP)
+        total_flops=2.0 * n_valid * D * vocab + 6.0 * n_bwd * D * vocab, dense_flops=8.0 * n_valid * D * vocab,
+        out_shape=(args.batch, RESP), metric=METRIC if vocab == V else f"{METRIC} [tuning: vocab {vocab}]",
+        config=config_dict(args.batch, n_valid, world, args.softcap, vocab),
+        traffic_ok=world == 1 and vocab == V and args.batch == B and args.softcap == SOFTCAP)
 
 
 def dense_workload(args, dev, rank, world, mesh, softcap, chunk, T_cfg):
     from gemma4_posttrain_jax_b200.losses import per_token_logps
 
     _, d_model, frozen, second_pass = DENSE_CONFIGS[args.config]
-    vs = V // world
+    vs = args.vocab_per_gpu or V // world
+    vocab = vs * world
     gen = torch.Generator(device=dev).manual_seed(SEED + 1)
-    W_full = (torch.randn((V, d_model), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    W_full = (torch.randn((vocab, d_model), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
     W = W_full[rank * vs : (rank + 1) * vs].clone().requires_grad_(not frozen)
     W2 = None
     if second_pass:  # old / reference policy head: W + N(0, 1e-4)
@@ -532,7 +538,7 @@ def dense_workload(args, dev, rank, world, mesh, softcap, chunk, T_cfg):
     del W_full
     gen_h = torch.Generator(device=dev).manual_seed(SEED + 2)
     Hd = torch.randn((T_cfg, d_model), generator=gen_h, device=dev).to(torch.bfloat16)
-    Yd = torch.randint(0, V, (T_cfg,), generator=gen_h, device=dev, dtype=torch.int32)
+    Yd = torch.randint(0, vocab, (T_cfg,), generator=gen_h, device=dev, dtype=torch.int32)
     Gd = torch.randn((T_cfg,), generator=gen_h, device=dev)
 
     def step(Hx, Yx, Gx):
@@ -556,14 +562,14 @@ def dense_workload(args, dev, rank, world, mesh, softcap, chunk, T_cfg):
              "bwd_dz_gemm": 2.0 * T_cfg * d_model * vs, "bwd_dh_gemm": 2.0 * T_cfg * d_model * vs}
     if not frozen:
         flops["bwd_dw_gemm"] = 2.0 * T_cfg * d_model * vs
-    total = (2.0 * (2 if second_pass else 1) + (4.0 if frozen else 6.0)) * T_cfg * d_model * V
+    total = (2.0 * (2 if second_pass else 1) + (4.0 if frozen else 6.0)) * T_cfg * d_model * vocab
     cfg = {"workload": f"BASELINE config {args.config}: {DENSE_NAMES[args.config]}", "tokens": T_cfg,
-           "hidden": d_model, "vocab": V, "vocab_per_gpu": vs, "softcap": args.softcap if args.softcap > 0 else None,
+           "hidden": d_model, "vocab": vocab, "vocab_per_gpu": vs, "softcap": args.softcap if args.softcap > 0 else None,
            "parallelism": f"vocab{world}", "l2": "no flush: W shard exceeds the 126 MB L2"}
     return Workload(
         W=W, inputs=[Hd, Yd, Gd], step=step, parity_view=parity_view, n_valid=T_cfg, n_bwd=T_cfg, d=d_model, vs=vs,
         flops=flops, total_flops=total, dense_flops=total, out_shape=(T_cfg,),
-        metric=f"logprob tokens/s @V=262144,d={d_model} (BASELINE config {args.config}, vocab-sharded)", config=cfg,
+        metric=f"logprob tokens/s @V={vocab},d={d_model} (BASELINE config {args.config}, vocab-sharded)", config=cfg,
         traffic_ok=False)
 
 

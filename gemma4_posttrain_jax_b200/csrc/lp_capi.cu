@@ -132,9 +132,22 @@ enum CgUse { CG_FWD, CG_DZ, CG_DH, CG_DW, CG_HOOK };
 int cta_group_for(CgUse k) {
   const int f = forced_cta_group();
   if (f) return f;
+  // tuning: LP_B200_CG_PER_GEMM="fzhw" (four digits 1 / 2: forward, dZ, dH, dW)
+  static const char* per = getenv("LP_B200_CG_PER_GEMM");
+  if (per != nullptr && k < CG_HOOK && (int)strlen(per) >= 4 && (per[k] == '1' || per[k] == '2')) return per[k] - '0';
   return (k == CG_DH || k == CG_DW) ? 2 : 1;
 }
 int cta_group() { return forced_cta_group(); }
+
+// The dW GEMM's K is the chunk's token count. With few tokens (e.g. T = 256) each tile is a
+// few K blocks and the pair's cross-SM hand-offs (both CTAs' loads, both epilogues) are not
+// amortised: single CTAs measured faster there (T = 256: 0.35 vs 0.43 ms, the bf16 dW stores
+// at 0.86 of the write-only HBM bandwidth), pairs faster at thousands of tokens.
+int cta_group_dw(int64_t k_tokens) {
+  const int cg = cta_group_for(CG_DW);
+  if (forced_cta_group() != 0 || getenv("LP_B200_CG_PER_GEMM") != nullptr) return cg;
+  return k_tokens <= 1024 ? 1 : cg;
+}
 
 struct DeviceInfo {
   int sms = 0;
@@ -296,18 +309,22 @@ bool mn3d_enabled() {
   return on;
 }
 
-// Epilogue store targets: one 32-row x 64-byte box per warp and piece, 64-byte swizzle
-// (32 bf16 or 16 f32 columns), matching the staging layout of the GEMM epilogue.
+// Epilogue store targets: one 32-row box per warp and piece, rows of `box_row_bytes` (64 or
+// 128, the store_row_bytes of the GEMM) with the swizzle of that width, matching the staging
+// layout of the GEMM epilogue.
 int map_store_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
-                   const char* what) {
-  return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, outer, ld_elems * 2, 32, 32, what,
-                  CU_TENSOR_MAP_SWIZZLE_64B);
+                   const char* what, int box_row_bytes = 64) {
+  return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, outer, ld_elems * 2, box_row_bytes / 2, 32,
+                  what, box_row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
 }
 int map_store_f32(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
-                  const char* what) {
-  return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, inner, outer, ld_elems * 4, 16, 32, what,
-                  CU_TENSOR_MAP_SWIZZLE_64B);
+                  const char* what, int box_row_bytes = 64) {
+  return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, inner, outer, ld_elems * 4, box_row_bytes / 4, 32,
+                  what, box_row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
 }
+
+// store_row_bytes of the plain-store GEMM (EPI_STORE) at CTA group cg.
+int store_box_bytes(int cg) { return cg == 2 ? store_row_bytes<2, EPI_STORE>() : store_row_bytes<1, EPI_STORE>(); }
 
 // --------------------------------------------------------------------------- planning
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -371,13 +388,18 @@ GemmSched plan_gemm(int64_t M, int64_t N, int64_t K, int sms, bool allow_split, 
   // Concurrent units stream shared operands through L2; a unit longer than ~1024 K blocks
   // lets CTAs drift apart by more than L2 holds, so long K ranges are split.
   const int64_t kb_cap = 1024;
+  // A split writes f32 partials that a separate pass reads back: S * M * N * 4 bytes each way,
+  // charged in units of one K block's time on one worker (~512 cycles, in which the GPU
+  // moves ~2 MB through HBM).
+  const double reduce_units_per_split = (double)M * (double)N * 8.0 / (2.0 * 1024 * 1024);
   for (int sp = 1; sp <= smax; ++sp) {
     const int64_t kb = cdiv(s.k_blocks, sp);
     if (sp > 1 && kb < 8) break;
     if (allow_split && kb > kb_cap) continue;
     const int64_t real_splits = cdiv(s.k_blocks, kb);
     if (real_splits != sp) continue;
-    const double c = (double)cdiv(tiles * sp, sms) * kb * (1.0 + 0.02 * (sp > 1));
+    const double c = (double)cdiv(tiles * sp, sms) * kb * (1.0 + 0.02 * (sp > 1)) +
+                     (sp > 1 ? sp * reduce_units_per_split : 0.0);
     if (c < best * 0.995) {
       best = c;
       best_s = sp;
@@ -389,18 +411,29 @@ GemmSched plan_gemm(int64_t M, int64_t N, int64_t K, int sms, bool allow_split, 
   return s;
 }
 
-// Backward token chunk: dZ (bf16 [chunk, Vs]) is the backward's only [T, V]-shaped buffer,
-// so its size bounds the chunk (LP_B200_DZ_CHUNK_MB, default 4096 MB). Chunks are of equal
-// size on 256-row boundaries: a short last chunk leaves most SMs idle at the end of each of
-// its three GEMMs.
-int64_t default_token_chunk(int64_t T, int64_t Vs) {
+// Backward token chunk. Two bounds (measured on the config-2 batch):
+//  - dZ (bf16 [chunk, Vs]) is the backward's only [T, V]-shaped buffer: at most 4 GiB of it
+//    (LP_B200_DZ_CHUNK_MB); larger chunks at Vs = 262144 made every backward GEMM slower;
+//  - the chunk's hidden rows (bf16 [chunk, d]) are re-read from L2 for every vocabulary tile
+//    by the dZ GEMM and for every row block of dW by the dW GEMM: at most 64 MB of them
+//    (LP_B200_H_CHUNK_MB), so they stay in the 126 MB L2. This bound is the one that binds
+//    for small shards (Vs = 32768 at 8 GPUs: 16384 rows instead of 65536).
+// Chunks are of equal size on 256-row boundaries: a short last chunk leaves most SMs idle
+// at the end of each of its three GEMMs.
+int64_t default_token_chunk(int64_t T, int64_t Vs, int64_t d) {
   static const int64_t budget = [] {
     const char* e = getenv("LP_B200_DZ_CHUNK_MB");
     const long long mb = (e != nullptr && atoll(e) > 0) ? atoll(e) : 4096;
     return (int64_t)mb << 20;
   }();
+  static const int64_t h_budget = [] {
+    const char* e = getenv("LP_B200_H_CHUNK_MB");
+    const long long mb = (e != nullptr && atoll(e) > 0) ? atoll(e) : 64;
+    return (int64_t)mb << 20;
+  }();
   const int64_t ldz = (Vs + 7) / 8 * 8;
-  const int64_t cap = std::max<int64_t>(256, budget / (ldz * 2) / 256 * 256);
+  const int64_t rows = std::min(budget / (ldz * 2), h_budget / std::max<int64_t>(2 * d, 1));
+  const int64_t cap = std::max<int64_t>(256, rows / 256 * 256);
   if (T <= cap) return std::max<int64_t>(T, 1);
   const int64_t chunks = cdiv(T, cap);
   return std::min<int64_t>(cap, cdiv(cdiv(T, chunks), 256) * 256);
@@ -415,7 +448,7 @@ struct BwdLayout {
 
 BwdLayout bwd_layout(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int flags, int sms, int bm) {
   BwdLayout L{};
-  L.tc = token_chunk > 0 ? std::min<int64_t>(token_chunk, std::max<int64_t>(T, 1)) : default_token_chunk(T, Vs);
+  L.tc = token_chunk > 0 ? std::min<int64_t>(token_chunk, std::max<int64_t>(T, 1)) : default_token_chunk(T, Vs, d);
   L.chunks = T > 0 ? cdiv(T, L.tc) : 0;
   L.ldz = (Vs + 7) / 8 * 8;
   L.mpad = cdiv(L.tc, bm) * bm;
@@ -952,10 +985,10 @@ int bwd_impl(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, con
     if (want_dw) LP_CUDA_TRY(cudaMemsetAsync(dW, 0, (size_t)Vs * d * (dw_bf16 ? 2 : 4), st));
     return LP_OK;
   }
-  const int cg_dz = cta_group_for(CG_DZ), cg_dh = cta_group_for(CG_DH), cg_dw = cta_group_for(CG_DW);
+  const int cg_dz = cta_group_for(CG_DZ), cg_dh = cta_group_for(CG_DH);
   if (ms != nullptr && want_dh) {
     // chunks start on 256-row boundaries (the row-block counters are per 128 rows)
-    if (token_chunk <= 0) token_chunk = default_token_chunk(T, Vs);
+    if (token_chunk <= 0) token_chunk = default_token_chunk(T, Vs, d);
     if (token_chunk < T) token_chunk = std::max<int64_t>(256, token_chunk / 256 * 256);
   }
   const BwdLayout L = bwd_layout(T, d, Vs, token_chunk, flags, workers(di, cg_dh), 128 * cg_dh);
@@ -1007,7 +1040,7 @@ int bwd_impl(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, con
       if (ms != nullptr) {
         // partial tiles stored (bf16) into this rank's copy, summed across ranks by the
         // reduce items of the same launch
-        if ((rc = map_store_bf16(&to, dh_c, d, tcur, ld_dh, "dH partial store"))) return rc;
+        if ((rc = map_store_bf16(&to, dh_c, d, tcur, ld_dh, "dH partial store", store_box_bytes(cg_dh)))) return rc;
         p.e.store_mode = STORE_BF16;
         p.e.split_rows = 0;
         p.s.red_lag = std::min(p.s.tiles_m, (int)cdiv(3 * (int64_t)wk, p.s.tiles_n) + 2);
@@ -1023,15 +1056,17 @@ int bwd_impl(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, con
         p.e.peer_limit_ns = ms->limit_ns;
       } else if (p.s.k_splits == 1) {
         if (dh_f32) {
-          if ((rc = map_store_f32(&to, dh_c, d, tcur, ld_dh, "dH store"))) return rc;
+          if ((rc = map_store_f32(&to, dh_c, d, tcur, ld_dh, "dH store", store_box_bytes(cg_dh)))) return rc;
           p.e.store_mode = STORE_F32;
         } else {
-          if ((rc = map_store_bf16(&to, dh_c, d, tcur, ld_dh, "dH store"))) return rc;
+          if ((rc = map_store_bf16(&to, dh_c, d, tcur, ld_dh, "dH store", store_box_bytes(cg_dh)))) return rc;
           p.e.store_mode = STORE_BF16;
         }
         p.e.split_rows = 0;
       } else {
-        if ((rc = map_store_f32(&to, part, d, (uint64_t)p.s.k_splits * L.mpad, d, "dH partials"))) return rc;
+        if ((rc = map_store_f32(&to, part, d, (uint64_t)p.s.k_splits * L.mpad, d, "dH partials",
+                                store_box_bytes(cg_dh))))
+          return rc;
         p.e.store_mode = STORE_F32;
         p.e.split_rows = (int)L.mpad;
       }
@@ -1047,6 +1082,7 @@ int bwd_impl(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, con
     }
     // 3) dW (+)= dZ^T . H_chunk
     if (want_dw) {
+      const int cg_dw = cta_group_dw(tcur);
       alignas(64) CUtensorMap ta, tb, to;
       GemmParams p{};
       p.a_mn3d = mn3d_enabled() && Vs % 64 == 0;
@@ -1060,10 +1096,10 @@ int bwd_impl(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, con
       p.s = plan_gemm(Vs, d, tcur, workers(di, cg_dw), false, 1, 128 * cg_dw);
       const bool direct_bf16 = dw_bf16 && L.chunks == 1;
       if (direct_bf16) {
-        if ((rc = map_store_bf16(&to, dW, d, Vs, d, "dW store"))) return rc;
+        if ((rc = map_store_bf16(&to, dW, d, Vs, d, "dW store", store_box_bytes(cg_dw)))) return rc;
         p.e.store_mode = STORE_BF16;
       } else {
-        if ((rc = map_store_f32(&to, dw_acc, d, Vs, d, "dW store"))) return rc;
+        if ((rc = map_store_f32(&to, dw_acc, d, Vs, d, "dW store", store_box_bytes(cg_dw)))) return rc;
         p.e.store_mode = c == 0 ? STORE_F32 : STORE_F32_ADD;
       }
       set_hints(p, G_DW);
@@ -1130,7 +1166,7 @@ int lp_gemm_bf16(void* stream, const void* A, int64_t M, int64_t K, int64_t lda,
   if (b_mn) rc = map_bf16(&tb, B, N, K, ldb, 64, 64, "B (MN-major)");
   else rc = map_bf16(&tb, B, K, N, ldb, BK, b_box_rows(cg), "B (K-major)");
   if (rc) return rc;
-  if ((rc = map_store_f32(&to, D, N, M, ldd, "D"))) return rc;
+  if ((rc = map_store_f32(&to, D, N, M, ldd, "D", store_box_bytes(cg)))) return rc;
   GemmParams p{};
   p.s = plan_gemm(M, N, K, workers(di, cg), false, 0, 128 * cg);
   p.e.store_mode = STORE_F32;

@@ -43,7 +43,8 @@
 #include "lp_ptx.cuh"
 
 // Shared-memory ring depth per CTA group: the largest that fits 227 KB with the epilogue
-// staging (single CTAs: 4 x 48 KB, pairs: 6 x 32 KB). Measured (pipeline counters, config-2
+// staging (single CTAs: 4 x 48 KB; pairs: 6 x 32 KB, or 5 x 32 KB beside the 64 KB of
+// 128-byte store staging of the plain-store GEMMs). Measured (pipeline counters, config-2
 // workload): the single-CTA forward waits 639 / 207 / 103 cycles per K block for its loads
 // with 2 / 3 / 4 stages; the pairs gain nothing from a 6th stage over 5. Overridable at
 // build time for tuning.
@@ -52,6 +53,9 @@
 #endif
 #ifndef LP_STAGES_CG2
 #define LP_STAGES_CG2 6
+#endif
+#ifndef LP_STAGES_CG2_STORE
+#define LP_STAGES_CG2_STORE 5
 #endif
 
 namespace lpk {
@@ -62,8 +66,6 @@ constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int A_STAGE_BYTES = 128 * BK * 2;                // 16 KB: 128 rows of A per CTA
-constexpr int STAGING_BUF_BYTES = 32 * 64;                 // 32 rows x 64 B, one TMA box
-constexpr int STAGING_WARP_BYTES = 2 * STAGING_BUF_BYTES;  // double-buffered per warp
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -76,8 +78,26 @@ struct Cfg {
   static constexpr int B_ROWS = BN / CG;                   // rows of B staged by each CTA
   static constexpr int B_STAGE_BYTES = B_ROWS * BK * 2;    // 32 KB (CG=1) / 16 KB (CG=2)
   static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
-  static constexpr int NUM_STAGES = CG == 1 ? LP_STAGES_CG1 : LP_STAGES_CG2;
 };
+
+// Epilogue TMA store box: 32 rows x store_row_bytes (64 B with 64-byte swizzle, or 128 B
+// with 128-byte swizzle). The plain-store pair GEMMs (dH, dW) use 128-byte rows: half the
+// store instructions per tile and whole 128-byte lines per row; the others keep 64-byte
+// rows, which leave room for a deeper operand ring.
+template <int CG, int EPI>
+__host__ __device__ constexpr int store_row_bytes() {
+  return (EPI == EPI_STORE && CG == 2) ? 128 : 64;
+}
+
+template <int CG, int EPI>
+__host__ __device__ constexpr int staging_buf_bytes() {
+  return 32 * store_row_bytes<CG, EPI>();
+}
+
+template <int CG, int EPI>
+__host__ __device__ constexpr int num_stages() {
+  return CG == 1 ? LP_STAGES_CG1 : (EPI == EPI_STORE ? LP_STAGES_CG2_STORE : LP_STAGES_CG2);
+}
 
 struct GemmSched {
   int M, N, K;
@@ -225,20 +245,39 @@ __host__ __device__ __forceinline__ Unit get_unit(const GemmSched& s, int u) {
   return x;
 }
 
-template <int EPI>
+template <int CG, int EPI>
 __host__ __device__ constexpr int staging_bytes() {
-  return EPI == EPI_FWD_LSE ? 0 : EPI_WARPS * STAGING_WARP_BYTES;
+  // double-buffered box per epilogue warp
+  return EPI == EPI_FWD_LSE ? 0 : EPI_WARPS * 2 * staging_buf_bytes<CG, EPI>();
 }
 
 template <int CG, int EPI>
 __host__ __device__ constexpr int gemm_smem_bytes() {
   // 1 KB alignment slack + stages + staging + barriers, work-unit ring, TMEM slot, abort flag
-  return 1024 + Cfg<CG>::NUM_STAGES * Cfg<CG>::STAGE_BYTES + staging_bytes<EPI>() + 512;
+  return 1024 + num_stages<CG, EPI>() * Cfg<CG>::STAGE_BYTES + staging_bytes<CG, EPI>() + 512;
 }
+
+// Every kernel variant fits the 227 KB of dynamic shared memory a CTA may use.
+static_assert(gemm_smem_bytes<1, EPI_FWD_LSE>() <= 232448 && gemm_smem_bytes<1, EPI_BWD_DZ>() <= 232448 &&
+                  gemm_smem_bytes<1, EPI_STORE>() <= 232448 && gemm_smem_bytes<1, EPI_HEAD>() <= 232448 &&
+                  gemm_smem_bytes<2, EPI_FWD_LSE>() <= 232448 && gemm_smem_bytes<2, EPI_BWD_DZ>() <= 232448 &&
+                  gemm_smem_bytes<2, EPI_STORE>() <= 232448 && gemm_smem_bytes<2, EPI_HEAD>() <= 232448,
+              "GEMM shared memory above 227 KB");
 
 // Byte offset of 16-byte chunk c (0..3) of row r in a 64-byte-swizzled box of 64-byte rows
 // (the TMA SWIZZLE_64B pattern: address bits [4,6) ^= bits [7,9)); 512-byte aligned box.
 __device__ __forceinline__ uint32_t sw64_offset(int r, int c) { return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
+
+// The same for chunk c (0..7) of a 128-byte-swizzled box of 128-byte rows (SWIZZLE_128B:
+// address bits [4,7) ^= bits [7,10)); 1024-byte aligned box. Eight consecutive rows put a
+// given chunk in eight different bank groups, so a warp's 16-byte stores do not conflict.
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+template <int RB>
+__device__ __forceinline__ uint32_t staging_offset(int r, int c) {
+  if constexpr (RB == 128) return sw128_offset(r, c);
+  else return sw64_offset(r, c);
+}
 
 // ----------------------------------------------------------------------------- kernel
 template <int CG, int EPI, bool A_MN, bool B_MN, bool HAS_CAP>
@@ -246,12 +285,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const GemmParams P) {
   using C = Cfg<CG>;
-  constexpr int NS = C::NUM_STAGES;
+  constexpr int NS = num_stages<CG, EPI>();
+  constexpr int SBUF = staging_buf_bytes<CG, EPI>();  // one staging box
+  constexpr int RB = store_row_bytes<CG, EPI>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
   uint8_t* staging = smem + NS * C::STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + staging_bytes<EPI>());
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + staging_bytes<CG, EPI>());
   uint64_t* full_bar = bars;             // [NS]
   uint64_t* empty_bar = bars + NS;       // [NS]
   uint64_t* tfull_bar = bars + 2 * NS;   // [2]
@@ -538,7 +579,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int ew = warp - 2;
     const int h = ew / 4;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    uint8_t* my_staging = staging + ew * STAGING_WARP_BYTES;
+    uint8_t* my_staging = staging + ew * 2 * SBUF;
     int sb = 0;
     uint32_t tc = 0;
     const EpiParams& E = P.e;
@@ -703,7 +744,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
             if (lane == 0) bulk_wait_read<1>();
             __syncwarp();
-            uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
+            uint8_t* buf_s = my_staging + sb * SBUF;
             const uint32_t sbase = smem_u32(buf_s);
 #pragma unroll
             for (int c = 0; c < 4; ++c)
@@ -755,7 +796,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (E.store_logits && nvalid > 0) {
               if (lane == 0) bulk_wait_read<1>();
               __syncwarp();
-              uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
+              uint8_t* buf_s = my_staging + sb * SBUF;
               const uint32_t sbase = smem_u32(buf_s);
 #pragma unroll
               for (int c = 0; c < 4; ++c)
@@ -772,51 +813,63 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         } else {  // EPI_STORE
           const int row0 = un.split * E.split_rows + row_base;
           if (E.store_mode == STORE_BF16) {
+            constexpr int COLS = RB / 2;  // bf16 columns per box
 #pragma unroll 1
-            for (int pc = 0; pc < BN / 64; ++pc) {
-              uint32_t r[32];
-              __syncwarp();
-              tmem_ld32(taddr + pc * 32, r);
-              tmem_wait_ld(r);
-              uint32_t pk[16];
+            for (int pc = 0; pc < (BN / 2) / COLS; ++pc) {
+              uint32_t pk[COLS / 2];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+              for (int q = 0; q < COLS / 32; ++q) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld32(taddr + pc * COLS + q * 32, r);
+                tmem_wait_ld(r);
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                  pk[q * 16 + j] = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+              }
               if (lane == 0) bulk_wait_read<1>();
               __syncwarp();
-              uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
+              uint8_t* buf_s = my_staging + sb * SBUF;
               const uint32_t sbase = smem_u32(buf_s);
 #pragma unroll
-              for (int c = 0; c < 4; ++c)
-                st_shared_v4(sbase + sw64_offset(lane, c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+              for (int c = 0; c < RB / 16; ++c)
+                st_shared_v4(sbase + staging_offset<RB>(lane, c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
+                             pk[4 * c + 3]);
               fence_proxy_async_smem();
               __syncwarp();
               if (lane == 0) {
-                tma_store_2d(&tmO, buf_s, colh + pc * 32, row0);
+                tma_store_2d(&tmO, buf_s, colh + pc * COLS, row0);
                 bulk_commit();
               }
               sb ^= 1;
             }
           } else {
+            constexpr int COLS = RB / 4;  // f32 columns per box
 #pragma unroll 1
-            for (int pc = 0; pc < BN / 32; ++pc) {
-              uint32_t r[16];
+            for (int pc = 0; pc < (BN / 2) / COLS; ++pc) {
+              uint32_t r[COLS];
               __syncwarp();
-              tmem_ld16(taddr + pc * 16, r);
-              tmem_wait_ld16(r);
+              if constexpr (COLS == 32) {
+                tmem_ld32(taddr + pc * COLS, r);
+                tmem_wait_ld(r);
+              } else {
+                tmem_ld16(taddr + pc * COLS, r);
+                tmem_wait_ld16(r);
+              }
               if (lane == 0) bulk_wait_read<1>();
               __syncwarp();
-              uint8_t* buf_s = my_staging + sb * STAGING_BUF_BYTES;
+              uint8_t* buf_s = my_staging + sb * SBUF;
               const uint32_t sbase = smem_u32(buf_s);
 #pragma unroll
-              for (int c = 0; c < 4; ++c)
-                st_shared_v4(sbase + sw64_offset(lane, c), r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+              for (int c = 0; c < RB / 16; ++c)
+                st_shared_v4(sbase + staging_offset<RB>(lane, c), r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
               fence_proxy_async_smem();
               __syncwarp();
               if (lane == 0) {
                 if (E.store_mode == STORE_F32_ADD)
-                  tma_reduce_add_2d(&tmO, buf_s, colh + pc * 16, row0);
+                  tma_reduce_add_2d(&tmO, buf_s, colh + pc * COLS, row0);
                 else
-                  tma_store_2d(&tmO, buf_s, colh + pc * 16, row0);
+                  tma_store_2d(&tmO, buf_s, colh + pc * COLS, row0);
                 bulk_commit();
               }
               sb ^= 1;
