@@ -79,6 +79,9 @@ def check_per_token(mesh, dev, rank, world, mode, V, T, d, seed, stats_mode="mul
                   f"dH rel-L2 {e_h:.2e}, dW rel-L2 {e_w:.2e}, skipped rows zero: {zero_rows}, "
                   f"logps identical across exchanges: {same}", flush=True)
             ok = ok and e_lp <= 2e-3 and e_h <= 1e-2 and e_w <= 1e-2 and zero_rows and same
+        # the other ranks wait here (host side) while rank 0 runs the CPU oracle, not inside
+        # the next call's bounded device-side wait for rank 0
+        dist.barrier(device_ids=[dev.index])
     return ok
 
 
