@@ -14,6 +14,7 @@
 
 #include "../../include/lp_logprob.h"
 #include "lp_gemm.cuh"
+#include "lp_plan.cuh"
 #include "lp_small_kernels.cuh"
 
 namespace {
@@ -326,152 +327,7 @@ int map_store_f32(CUtensorMap* m, const void* base, uint64_t inner, uint64_t out
 // store_row_bytes of the plain-store GEMM (EPI_STORE) at CTA group cg.
 int store_box_bytes(int cg) { return cg == 2 ? store_row_bytes<2, EPI_STORE>() : store_row_bytes<1, EPI_STORE>(); }
 
-// --------------------------------------------------------------------------- planning
-int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
-size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
-
-// Forward plan. The forward reads every H row block once per vocabulary tile, so the H rows
-// that concurrent CTAs re-read must stay in L2: units walk the tokens in chunks of about
-// 12288 rows (48 MB of bf16 H at d = 2048), and within a chunk all vocabulary groups
-// before the next chunk. Each unit covers G consecutive vocabulary tiles; G keeps the
-// per-row (max, sum) partials ([n_groups, T] float2) under ~128 MB.
-GemmSched plan_fwd(int64_t T, int64_t Vs, int64_t d, int workers, int bm) {
-  GemmSched s{};
-  s.bm = bm;
-  s.M = (int)T;
-  s.N = (int)Vs;
-  s.K = (int)d;
-  s.tiles_m = (int)cdiv(T, bm);
-  s.tiles_n = (int)cdiv(Vs, BN);
-  s.k_blocks = (int)cdiv(d, BK);
-  s.k_splits = 1;
-  s.kb_per_split = s.k_blocks;
-  s.n_fast = 0;
-  static const char* chunk_env = getenv("LP_B200_FWD_CHUNK_MB");  // tuning: H chunk size
-  const int64_t chunk_mb = (chunk_env != nullptr && atoi(chunk_env) > 0) ? atoi(chunk_env) : 48;
-  const int64_t chunk_rows = std::max<int64_t>(bm, (chunk_mb << 20) / std::max<int64_t>(2 * d, 1));
-  s.m_chunk = (int)std::max<int64_t>(1, chunk_rows / bm);
-  static const char* no_chunk = getenv("LP_B200_FWD_NO_CHUNK");  // tuning: plain M-fast order
-  if (no_chunk != nullptr && no_chunk[0] == '1') s.m_chunk = 0;
-  const int64_t part_cap = int64_t(128) << 20;
-  int g = 1;
-  while (g < s.tiles_n && 2 * cdiv(s.tiles_n, g) * T * 8 > part_cap) g *= 2;
-  // at least a few tiles per unit so the per-unit epilogue state amortises
-  g = std::max(g, std::min(4, s.tiles_n));
-  static const char* force_g = getenv("LP_B200_FWD_GROUP");  // tuning: tiles per unit
-  if (force_g != nullptr && atoi(force_g) > 0) g = std::min(atoi(force_g), s.tiles_n);
-  (void)workers;
-  s.n_group = g;
-  s.n_groups = (int)cdiv(s.tiles_n, g);
-  s.num_units = s.tiles_m * s.n_groups;
-  return s;
-}
-
-// Plain GEMM with optional split-K: pick S in [1, 16] minimising the critical path,
-// keeping at least 8 K blocks per split; ties prefer fewer splits.
-GemmSched plan_gemm(int64_t M, int64_t N, int64_t K, int sms, bool allow_split, int n_fast, int bm) {
-  GemmSched s{};
-  s.bm = bm;
-  s.M = (int)M;
-  s.N = (int)N;
-  s.K = (int)K;
-  s.tiles_m = (int)cdiv(M, bm);
-  s.tiles_n = (int)cdiv(N, BN);
-  s.k_blocks = (int)cdiv(K, BK);
-  s.n_group = 1;
-  s.n_groups = s.tiles_n;
-  s.n_fast = n_fast;
-  const int64_t tiles = (int64_t)s.tiles_m * s.tiles_n;
-  int best_s = 1;
-  double best = 1e300;
-  const int smax = allow_split ? 64 : 1;
-  // Concurrent units stream shared operands through L2; a unit longer than ~1024 K blocks
-  // lets CTAs drift apart by more than L2 holds, so long K ranges are split.
-  const int64_t kb_cap = 1024;
-  // A split writes f32 partials that a separate pass reads back: S * M * N * 4 bytes each way,
-  // charged in units of one K block's time on one worker (~512 cycles, in which the GPU
-  // moves ~2 MB through HBM).
-  const double reduce_units_per_split = (double)M * (double)N * 8.0 / (2.0 * 1024 * 1024);
-  for (int sp = 1; sp <= smax; ++sp) {
-    const int64_t kb = cdiv(s.k_blocks, sp);
-    if (sp > 1 && kb < 8) break;
-    if (allow_split && kb > kb_cap) continue;
-    const int64_t real_splits = cdiv(s.k_blocks, kb);
-    if (real_splits != sp) continue;
-    const double c = (double)cdiv(tiles * sp, sms) * kb * (1.0 + 0.02 * (sp > 1)) +
-                     (sp > 1 ? sp * reduce_units_per_split : 0.0);
-    if (c < best * 0.995) {
-      best = c;
-      best_s = sp;
-    }
-  }
-  s.kb_per_split = (int)cdiv(s.k_blocks, best_s);
-  s.k_splits = (int)cdiv(s.k_blocks, s.kb_per_split);
-  s.num_units = (int)(tiles * s.k_splits);
-  return s;
-}
-
-// Backward token chunk. Two bounds (measured on the config-2 batch):
-//  - dZ (bf16 [chunk, Vs]) is the backward's only [T, V]-shaped buffer: at most 4 GiB of it
-//    (LP_B200_DZ_CHUNK_MB); larger chunks at Vs = 262144 made every backward GEMM slower;
-//  - the chunk's hidden rows (bf16 [chunk, d]) are re-read from L2 for every vocabulary tile
-//    by the dZ GEMM and for every row block of dW by the dW GEMM: at most 64 MB of them
-//    (LP_B200_H_CHUNK_MB), so they stay in the 126 MB L2. This bound is the one that binds
-//    for small shards (Vs = 32768 at 8 GPUs: 16384 rows instead of 65536).
-// Chunks are of equal size on 256-row boundaries: a short last chunk leaves most SMs idle
-// at the end of each of its three GEMMs.
-int64_t default_token_chunk(int64_t T, int64_t Vs, int64_t d) {
-  static const int64_t budget = [] {
-    const char* e = getenv("LP_B200_DZ_CHUNK_MB");
-    const long long mb = (e != nullptr && atoll(e) > 0) ? atoll(e) : 4096;
-    return (int64_t)mb << 20;
-  }();
-  static const int64_t h_budget = [] {
-    const char* e = getenv("LP_B200_H_CHUNK_MB");
-    const long long mb = (e != nullptr && atoll(e) > 0) ? atoll(e) : 64;
-    return (int64_t)mb << 20;
-  }();
-  const int64_t ldz = (Vs + 7) / 8 * 8;
-  const int64_t rows = std::min(budget / (ldz * 2), h_budget / std::max<int64_t>(2 * d, 1));
-  const int64_t cap = std::max<int64_t>(256, rows / 256 * 256);
-  if (T <= cap) return std::max<int64_t>(T, 1);
-  const int64_t chunks = cdiv(T, cap);
-  return std::min<int64_t>(cap, cdiv(cdiv(T, chunks), 256) * 256);
-}
-
-struct BwdLayout {
-  int64_t tc, chunks, ldz;
-  size_t dz_off, part_off, dwacc_off, total;
-  int max_splits;
-  int64_t mpad;
-};
-
-BwdLayout bwd_layout(int64_t T, int64_t d, int64_t Vs, int64_t token_chunk, int flags, int sms, int bm) {
-  BwdLayout L{};
-  L.tc = token_chunk > 0 ? std::min<int64_t>(token_chunk, std::max<int64_t>(T, 1)) : default_token_chunk(T, Vs, d);
-  L.chunks = T > 0 ? cdiv(T, L.tc) : 0;
-  L.ldz = (Vs + 7) / 8 * 8;
-  L.mpad = cdiv(L.tc, bm) * bm;
-  // the largest split-K of any chunk (the first chunk is the largest)
-  L.max_splits = 1;
-  if (!(flags & LP_BWD_NO_DH) && T > 0) {
-    GemmSched s = plan_gemm(L.tc, d, Vs, sms, true, 1, bm);
-    L.max_splits = s.k_splits;
-    // a shorter last chunk may choose more splits
-    const int64_t last = T - (L.chunks - 1) * L.tc;
-    GemmSched s2 = plan_gemm(last, d, Vs, sms, true, 1, bm);
-    L.max_splits = std::max(L.max_splits, s2.k_splits);
-  }
-  size_t off = 0;
-  L.dz_off = off;
-  off += align_up((size_t)L.tc * L.ldz * 2, 1024);
-  L.part_off = off;
-  if (L.max_splits > 1) off += align_up((size_t)L.max_splits * L.mpad * d * 4, 1024);
-  L.dwacc_off = off;
-  if (!(flags & LP_BWD_NO_DW) && (flags & LP_BWD_DW_BF16) && L.chunks > 1) off += align_up((size_t)Vs * d * 4, 1024);
-  L.total = off;
-  return L;
-}
+// Planning (tile plans, split-K, backward token chunks, workspace layout): lp_plan.cuh.
 
 // --------------------------------------------------------------------------- launches
 }  // namespace
@@ -1015,7 +871,7 @@ int bwd_impl(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh, con
       if ((rc = map_bf16(&tb, W, d, Vs, d, BK, b_box_rows(cg_dz), "embedding"))) return rc;
       if ((rc = map_store_bf16(&to, dz, Vs, tcur, L.ldz, "dZ store"))) return rc;
       GemmParams p{};
-      p.s = plan_gemm(tcur, Vs, d, workers(di, cg_dz), false, 0, 128 * cg_dz);
+      p.s = plan_dz(tcur, Vs, d, workers(di, cg_dz), 128 * cg_dz);
       p.e.y = y + t0;
       p.e.v_off = v_off;
       p.e.softcap = softcap;
@@ -1327,10 +1183,6 @@ int noalloc_scratch(void** out) {
   return LP_OK;
 }
 
-size_t noalloc_fwd_bytes(const GemmSched& s, int64_t T, size_t* part_bytes) {
-  *part_bytes = align_up((size_t)2 * s.n_groups * T * sizeof(float2), 256);
-  return *part_bytes + align_up((size_t)T * 4, 256);
-}
 
 }  // namespace
 
@@ -1347,12 +1199,7 @@ extern "C" int lp_fwd_noalloc(void* stream, const void* H, int64_t T, int64_t d,
   const int cg = cta_group_for(CG_FWD);
   GemmSched s = plan_fwd(T, Vs, d, workers(di, cg), 128 * cg);
   size_t part_bytes = 0;
-  while (noalloc_fwd_bytes(s, T, &part_bytes) > kNoAllocScratchBytes && s.n_group < s.tiles_n) {
-    s.n_group = std::min(s.tiles_n, s.n_group * 2);
-    s.n_groups = (int)cdiv(s.tiles_n, s.n_group);
-    s.num_units = s.tiles_m * s.n_groups;
-  }
-  const size_t need = noalloc_fwd_bytes(s, T, &part_bytes);
+  const size_t need = widen_fwd_groups(&s, T, kNoAllocScratchBytes, &part_bytes);
   if (need > kNoAllocScratchBytes)
     return fail(LP_EINVAL,
                 "lp_fwd_noalloc: T=%lld tokens need %zu scratch bytes, above its fixed limit of %zu bytes "
