@@ -113,29 +113,21 @@ inline GemmSched plan_dz(int64_t M, int64_t Vs, int64_t d, int workers, int bm) 
   return s;
 }
 
-// Backward token chunk. Two bounds (measured on the config-2 batch):
-//  - dZ (bf16 [chunk, Vs]) is the backward's only [T, V]-shaped buffer: at most 4 GiB of it
-//    (LP_B200_DZ_CHUNK_MB); larger chunks at Vs = 262144 made every backward GEMM slower;
-//  - the chunk's hidden rows (bf16 [chunk, d]) are re-read from L2 for every vocabulary tile
-//    by the dZ GEMM and for every row block of dW by the dW GEMM: at most 64 MB of them
-//    (LP_B200_H_CHUNK_MB), so they stay in the 126 MB L2. This bound is the one that binds
-//    for small shards (Vs = 32768 at 8 GPUs: 16384 rows instead of 65536).
-// Chunks are of equal size on 256-row boundaries: a short last chunk leaves most SMs idle
-// at the end of each of its three GEMMs.
+// Backward token chunk: dZ (bf16 [chunk, Vs]) is the backward's only [T, V]-shaped buffer,
+// and at most 4 GiB of it (LP_B200_DZ_CHUNK_MB) is kept: larger chunks at Vs = 262144 drew
+// more power for no gain (16 GiB: 263.7k tokens/s at 1290 MHz vs 293.4k at 1395). The
+// hidden rows a chunk's dZ GEMM re-reads stay in L2 through its M-chunked unit order
+// (plan_dz), whatever the chunk size. Chunks are of equal size on 256-row boundaries: a
+// short last chunk leaves most SMs idle at the end of each of its three GEMMs.
 inline int64_t default_token_chunk(int64_t T, int64_t Vs, int64_t d) {
+  (void)d;
   static const int64_t budget = [] {
     const char* e = getenv("LP_B200_DZ_CHUNK_MB");
     const long long mb = (e != nullptr && atoll(e) > 0) ? atoll(e) : 4096;
     return (int64_t)mb << 20;
   }();
-  static const int64_t h_budget = [] {
-    const char* e = getenv("LP_B200_H_CHUNK_MB");
-    const long long mb = (e != nullptr && atoll(e) > 0) ? atoll(e) : 64;
-    return (int64_t)mb << 20;
-  }();
   const int64_t ldz = (Vs + 7) / 8 * 8;
-  const int64_t rows = std::min(budget / (ldz * 2), h_budget / std::max<int64_t>(2 * d, 1));
-  const int64_t cap = std::max<int64_t>(256, rows / 256 * 256);
+  const int64_t cap = std::max<int64_t>(256, budget / (ldz * 2) / 256 * 256);
   if (T <= cap) return std::max<int64_t>(T, 1);
   const int64_t chunks = cdiv(T, cap);
   return std::min<int64_t>(cap, cdiv(cdiv(T, chunks), 256) * 256);

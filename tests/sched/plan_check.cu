@@ -18,13 +18,13 @@ int main() {
   using namespace lpk;
   const int pairs = 74, sms = 148;
 
-  // config 2 (97,703 backward rows, d = 2048): at V = 262144 the dZ bound (4 GiB) gives 8192
-  // rows; at 32768 rows per shard (8 GPUs) the hidden-row bound (64 MB) gives 16384
+  // config 2 (97,703 backward rows): 4 GiB of dZ is 8192 rows at V = 262144 (12 chunks);
+  // at 32768 rows per shard (8 GPUs) it would be 65536, so two equal chunks of 48896
   CHECK(default_token_chunk(97703, 262144, 2048) == 8192);
-  CHECK(default_token_chunk(97703, 32768, 2048) == 16384);
+  CHECK(default_token_chunk(97703, 32768, 2048) == 48896);
   CHECK(default_token_chunk(97703, 131072, 2048) == 16384);
   CHECK(default_token_chunk(256, 262144, 2048) == 256);
-  CHECK(default_token_chunk(32768, 65536, 3840) == 8192);  // config 4 at 4 GPUs: 64 MB / 7680 B, 256-row multiple
+  CHECK(default_token_chunk(32768, 65536, 3840) == 32768);  // config 4 at 4 GPUs: one chunk
   // chunks are equal up to the 256-row rounding: no short tail
   for (int64_t T : {20000, 97703, 100001, 262144}) {
     for (int64_t Vs : {32768, 65536, 262144}) {
@@ -54,6 +54,14 @@ int main() {
     }
     const GemmSched n = plan_gemm(8192, 2048, 262144, pairs, false, 1, 256);  // mesh sum: no split
     CHECK(n.k_splits == 1);
+  }
+
+  // dZ recompute: no split, token chunks of 12288 rows (48 MB of hidden rows) walked chunk by
+  // chunk, every vocabulary tile of a chunk before the next
+  {
+    const GemmSched z = plan_dz(48896, 32768, 2048, sms, 128);
+    CHECK(z.k_splits == 1 && z.n_fast == 0 && z.m_chunk == 96);
+    CHECK(z.num_units == z.tiles_m * z.tiles_n);
   }
 
   // forward plan of config 2 at one GPU: 16 vocabulary tiles per unit (the partials stay
@@ -92,7 +100,7 @@ int main() {
     CHECK(L.max_splits >= 4);
     CHECK(L.total >= L.dwacc_off + (size_t)262144 * 2048 * 4);
     const BwdLayout M = bwd_layout(97703, 2048, 32768, 0, LP_BWD_DW_BF16, pairs, 256);
-    CHECK(M.tc == 16384 && M.chunks == 6 && M.max_splits == 1);
+    CHECK(M.tc == 48896 && M.chunks == 2 && M.max_splits == 1);
     const BwdLayout F = bwd_layout(256, 2048, 262144, 0, LP_BWD_DW_BF16, pairs, 256);
     CHECK(F.chunks == 1 && F.dwacc_off == F.total);  // one chunk: dW stored as bf16 directly
   }
