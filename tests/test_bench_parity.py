@@ -56,3 +56,51 @@ def test_float32_check_flags_wrong_results(what):
         c["dHv"][0] = 1.0  # row 0 has g == 0: its dH must be exactly zero
     r = _check(**c)
     assert not r["ok"], r
+
+
+def _parity_rank(rank, world, port, q):
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        c = _case(seed=9, V=800)
+        vs = 800 // world
+        W = c.pop("W")[rank * vs : (rank + 1) * vs]
+        c["dW"] = c["dW"][rank * vs : (rank + 1) * vs]
+        r = bench.parity_check(W, softcap=30.0, rank=rank, world=world, dev=torch.device("cpu"), rows=64, **c)
+        c["dHv"] = c["dHv"] * 1.05  # a wrong dH sum must fail on every rank
+        bad = bench.parity_check(W, softcap=30.0, rank=rank, world=world, dev=torch.device("cpu"), rows=64, **c)
+        q.put((rank, r["ok"], r["logp_max_abs"], r["dh_rel_l2"], r["dw_rel_l2"], bad["ok"]))
+        dist.destroy_process_group()
+    except Exception as exc:  # noqa: BLE001
+        q.put((rank, repr(exc), None, None, None, None))
+
+
+def test_float32_check_combines_shards_over_ranks():
+    """Two gloo ranks, each holding half of the vocabulary: the check's pmax / psum combine
+    and its summed dH rows reproduce the single-partition oracle, on both ranks alike."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_parity_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, e_lp, e_dh, e_dw, bad_ok in got:
+        assert ok is True, (rank, ok)
+        assert e_lp < 1e-5 and e_dh < 1e-5 and e_dw < 1e-5
+        assert bad_ok is False
+    assert got[0][2:5] == got[1][2:5]  # the reported errors are the same on every rank
