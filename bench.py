@@ -53,11 +53,13 @@ METRIC = "logprob fwd+bwd tokens/s @V=262144,d=2048 (GRPO response tokens, vocab
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch of the forward GEMM on this workload at N=1: a stored
 # constant, not measured by this run. It comes from an ncu capture of the batch-16 case of
-# this workload (``ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum
-# --clock-control none -k regex:tc_gemm -c 1 python bench.py --batch 16 --steps 1
-# --warmup 3 --no-e2e --no-cpu-baseline --no-parity``), scaled by the tokens of the full
-# batch (traffic grows in proportion to the token count at a fixed vocabulary).
-NCU_FWD_TRAFFIC_PER_TOKEN_N1 = 20.01e9 / 108376
+# this workload (13,969 tokens: 2.638 GB read + 0.061 GB written by the forward launch of
+# ``ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
+# --clock-control none -k regex:tc_gemm -s 39 -c 13 python bench.py --batch 16 --steps 1
+# --warmup 3 --no-e2e --no-cpu-baseline --no-parity --token-chunk 4096``), scaled by the
+# tokens of the full batch (the forward streams W once per 12,288-token block of hidden
+# rows, so its traffic grows in proportion to the token count at a fixed vocabulary).
+NCU_FWD_TRAFFIC_PER_TOKEN_N1 = (2.638e9 + 0.061e9) / 13969
 NCU_TRAFFIC_NOTE = "stored constant: ncu DRAM bytes of the forward GEMM per token (batch-16 capture), x tokens"
 LOGP_ATOL, GRAD_RTOL = 2e-3, 1e-2
 
