@@ -43,11 +43,13 @@ inline GemmSched plan_fwd(int64_t T, int64_t Vs, int64_t d, int workers, int bm)
   const int64_t part_cap = int64_t(128) << 20;
   int g = 1;
   while (g < s.tiles_n && 2 * cdiv(s.tiles_n, g) * T * 8 > part_cap) g *= 2;
-  // at least a few tiles per unit so the per-unit epilogue state amortises
+  // at least a few tiles per unit so the per-unit epilogue state amortises, unless that
+  // leaves fewer than four units per worker (few tokens: T = 256 has two M tiles)
+  const int g_part = g;
   g = std::max(g, std::min(4, s.tiles_n));
+  while (g > g_part && (int64_t)s.tiles_m * cdiv(s.tiles_n, g) < 4 * (int64_t)std::max(workers, 1)) g /= 2;
   static const char* force_g = getenv("LP_B200_FWD_GROUP");  // tuning: tiles per unit
   if (force_g != nullptr && atoi(force_g) > 0) g = std::min(atoi(force_g), s.tiles_n);
-  (void)workers;
   s.n_group = g;
   s.n_groups = (int)cdiv(s.tiles_n, g);
   s.num_units = s.tiles_m * s.n_groups;

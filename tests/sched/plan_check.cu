@@ -74,6 +74,15 @@ int main() {
     CHECK(fwd_scratch_bytes(f, 108376, &part) <= (size_t(129) << 20));
   }
 
+  // few tokens (config 1, T = 256: two M tiles): smaller groups, so the forward has at least
+  // four units per SM
+  {
+    const GemmSched f = plan_fwd(256, 262144, 2048, sms, 128);
+    CHECK(f.n_group == 2 && f.num_units == 1024);
+    const GemmSched h = plan_fwd(4096, 262144, 2048, sms, 128);  // 32 M tiles: the default 4 tiles
+    CHECK(h.n_group == 4);
+  }
+
   // fixed-scratch forward: groups widen until the partials fit 8 MiB
   {
     const size_t limit = size_t(8) << 20;
