@@ -115,11 +115,16 @@ def _backward_rows(embed, H, y, softcap, norm, g, *, mesh, vocab_offset, need_dh
     buf = dh_sum_buffer(mesh, rows, H.shape[-1], H.device) if (need_dh and P > 1) else None
     if buf is not None:
         timeout = peer_timeout_ms()
-        buf.counters[: int(ops.bwd_sum_counters(rows))].zero_()
-        ops.peer_barrier(buf, timeout)  # every rank's counters are zero and its previous dH read
+        # No barrier before the call: the counters are zero (zeroed at creation, and after each
+        # call, below), and another rank's sums reach this rank's dH copy only after this rank
+        # has started the call's dH GEMM, i.e. after it has consumed the previous dH.
         dH, dW = ops.shard_backward(embed, Hz, yz, softcap, nz, gz, vocab_offset=vocab_offset, need_dh=True,
                                     need_dw=need_dw, dh_dtype=torch.bfloat16, dw_dtype=dw_dtype,
                                     token_chunk=token_chunk, dh_mesh_sum=buf)
+        # Every rank reduces a share of every row block, so this rank's counters reached their
+        # final counts inside its dH GEMM: zeroed now, before the barrier that the next call's
+        # increments follow, they start the next call at zero.
+        buf.counters[: int(ops.bwd_sum_counters(rows))].zero_()
         with phase("dh_peer_barrier"):
             ops.peer_barrier(buf, timeout)  # every rank's share of the sum has landed everywhere
         _check_mesh_call(H.device, mesh, "lp_bwd_sum (dH summed over the mesh)")

@@ -210,9 +210,9 @@ def shard_backward(
     """``lp_bwd`` on one vocabulary shard: (dH [T, d] partial over this shard, dW [Vs, d]).
 
     With ``dh_mesh_sum`` (a ``sharding.DhSumBuffer`` with at least T rows; every rank makes
-    the same call between two ``peer_barrier`` calls, its counters zeroed before the first)
+    the same call, its counters zero, and zeroes them again and calls ``peer_barrier`` after it)
     this is ``lp_bwd_sum``: the returned dH is this rank's bf16 copy, which holds the sum over
-    the mesh's shards once the second barrier has passed.
+    the mesh's shards once that barrier has passed.
     """
     dev = _require_cuda(embed, hidden, targets, norm, grad_logp)
     _check_bf16("embedding", embed)

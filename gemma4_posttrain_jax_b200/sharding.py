@@ -227,6 +227,9 @@ class DhSumBuffer:
         self.dh = self.storage[: self.rows * self.d * 2].view(torch.bfloat16).view(self.rows, self.d)
         self.counters = self.storage[dh_bytes : dh_bytes + self.n_counters * 4].view(torch.int32)
         self.counters.zero_()
+        torch.cuda.synchronize(device)
+        # counters are zero on every rank before any rank's first lp_bwd_sum adds to them
+        _all_ranks_agree(mesh, True, device)
         mc = int(self.handle.multicast_ptr)
         # the same on every rank (same world size and signal pad size)
         if (_BARRIER_CHANNEL + 1) * self.handle.world_size * 4 > self.handle.signal_pad_size:

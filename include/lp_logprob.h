@@ -221,7 +221,11 @@ LP_API int lp_bwd(void* stream, const void* H, int64_t T, int64_t d, int64_t ldh
  *   dH / dH_multicast   this rank's address and the multicast address of a bf16 [T, ld_dh]
  *                       buffer bound on every rank (NVLS multicast object); 16-B aligned
  *   counters / counters_multicast  u32 [lp_bwd_sum_counters(T)] in the same kind of memory,
- *                       zeroed on every rank before the lp_peer_barrier preceding the call
+ *                       zero on every rank when the call starts: zero them once when the
+ *                       buffer is set up (before any rank's first call), and after each call
+ *                       on this rank's stream, before the lp_peer_barrier that follows it
+ *                       (every rank reduces a share of every row block, so its counters have
+ *                       reached their final counts when its call's dH GEMM ends)
  *   rank, world         this rank's position in the mesh and the mesh size
  *   timeout_ms          bound of every wait for the other ranks' tiles (device error on expiry)
  * Other arguments as lp_bwd (dH is always bf16; LP_BWD_DH_F32 / LP_BWD_NO_DH are rejected).
@@ -291,9 +295,10 @@ LP_API int lp_scatter_rows(void* stream, const void* src, int64_t src_stride, co
 
 /*
  * Device-side barrier of the `world` ranks of a vocabulary mesh, on `stream` (one small
- * kernel). It brackets lp_bwd_sum: one barrier before it (every rank has zeroed its
- * counters and finished reading its previous dH), one after it (every rank's multicast
- * stores have landed).
+ * kernel). It follows every lp_bwd_sum: when it passes, every rank's multicast stores have
+ * landed and every rank has zeroed its counters for the next call. No barrier is needed
+ * before lp_bwd_sum: another rank's sums reach this rank's copy only after this rank's own
+ * dH GEMM of the same call has started, i.e. after it has consumed its previous dH.
  *   signal_pads  device array [world] of u64: this process's address of each rank's
  *                signal pad (peer-mapped memory, u32 slots, zero-initialised)
  *   channel      slot row used: slots [channel * world, (channel + 1) * world) of each pad

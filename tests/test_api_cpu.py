@@ -159,9 +159,9 @@ def test_mesh_forward_routes_to_the_nvlink_exchange_or_the_all_gather(monkeypatc
 
 
 def test_mesh_backward_routes_the_dh_sum(monkeypatch):
-    """The backward of a vocabulary mesh: with a multicast dH buffer, zeroed counters, a peer
-    barrier, the fused lp_bwd_sum backward, a second barrier (dH shared with the buffer) and
-    the host-side check for a peer timeout;
+    """The backward of a vocabulary mesh: with a multicast dH buffer, the fused lp_bwd_sum
+    backward, the counters zeroed again for the next call, one peer barrier (dH shared with
+    the buffer) and the host-side check for a peer timeout;
     without one, the plain backward and an all-reduce of dH. Device calls are stubbed; only
     the routing and its order are checked."""
     import torch
@@ -198,7 +198,7 @@ def test_mesh_backward_routes_the_dh_sum(monkeypatch):
     dH, dW, pos, shared = losses._backward_rows(W, H, y, 30.0, norm, g, **kw)
     assert shared and pos is None
     # ... and the host waits for the stream, raising on a recorded peer timeout
-    assert calls == [("barrier", 777), ("lp_bwd_sum", 10, torch.bfloat16), ("barrier", 777), ("check", "lp_bwd_sum")]
+    assert calls == [("lp_bwd_sum", 10, torch.bfloat16), ("barrier", 777), ("check", "lp_bwd_sum")]
     assert buf.counters[:4].eq(0).all() and buf.counters[4:].eq(7).all()  # the used counters are zeroed
 
     calls.clear()
