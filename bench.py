@@ -15,7 +15,9 @@ A step = one call of the public API (``completion_logps``) + its backward on tha
 compaction, fused LM-head GEMM + online LSE, combine, recompute backward into dZ, dH and dW
 tensor-core GEMMs, scatter back. ``value`` has the inputs resident in HBM; ``e2e`` adds the
 host->device copy of every step's inputs (pinned; double-buffered, so step k+1's copy runs
-on the copy engines while step k computes) and the device->host read of the logps.
+on the copy engines while step k computes) and the device->host read of the logps. With
+N ranks each rank copies 1/N of the input bytes from host memory and pulls the other ranks'
+parts over NVLink (``StepLoader``), so the whole job moves the inputs across PCIe once.
 
 After the timed regions one more step is checked against a PyTorch float32 reference of
 the same arithmetic computed on the GPUs (``parity``): the logp of every token, dH on 256
@@ -575,8 +577,160 @@ def dense_workload(args, dev, rank, world, mesh, softcap, chunk, T_cfg):
         traffic_ok=False)
 
 
+# --------------------------------------------------------------------------- step-input loader
+def byte_parts(total: int, world: int, align: int = 256) -> list[int]:
+    """Bounds of ``world`` contiguous byte ranges covering ``total`` bytes, each starting on
+    an ``align``-byte boundary (rank r copies [b[r], b[r+1]) from host memory)."""
+    b = [min(total, -(-(total * r // world) // align) * align) for r in range(world)] + [total]
+    return b
+
+
+def pack_layout(inputs, align: int = 256):
+    """Byte offset of each input in one packed buffer, and the buffer's size."""
+    offs, pos = [], 0
+    for x in inputs:
+        pos = -(-pos // align) * align
+        offs.append(pos)
+        pos += x.nbytes
+    return offs, -(-pos // align) * align
+
+
+class StepLoader:
+    """Feeds every step's inputs from pinned host memory to the GPUs, as a data loader does.
+
+    The inputs are packed into one pinned host buffer and two device slots (double
+    buffering: step k+1's copies run while step k computes). With N > 1 ranks every rank
+    needs all of the inputs (they are replicated at the vocabulary-parallel boundary), but
+    only 1/N of the bytes cross PCIe on each rank: rank r copies its byte range from host
+    memory into its slot, and after a host barrier pulls the other ranks' ranges from their
+    slots over NVLink (copy-engine peer copies from symmetric memory; no kernel waits on a
+    peer). Without symmetric memory on every rank, every rank copies all bytes from host.
+
+    A background thread does the copies, so the host barrier and the peer copies overlap the
+    previous step's compute. Slot safety: step k's copies into slot k % 2 start once step
+    k - 2 (its last reader on this rank) has finished, and every rank's pulls of step k - 2
+    complete before the barrier of step k - 1, which comes before any rank overwrites its
+    range of that slot.
+    """
+
+    def __init__(self, inputs, *, dev, rank, world, gloo_group=None):
+        import torch.distributed as dist
+
+        self.dev, self.rank, self.world = dev, rank, world
+        self.offs, self.total = pack_layout(inputs)
+        self.host = torch.empty(self.total, dtype=torch.uint8).pin_memory()
+        for x, o in zip(inputs, self.offs):
+            self.host[o:o + x.nbytes].copy_(x.detach().contiguous().view(-1).view(torch.uint8).cpu())
+        self.sharded = False
+        self.slots, self.peers = [], []
+        if world > 1:
+            try:
+                import torch.distributed._symmetric_memory as symm_mem
+
+                slots = [symm_mem.empty((self.total,), dtype=torch.uint8, device=dev) for _ in range(2)]
+                ok = 1
+            except (RuntimeError, ImportError):  # includes torch.OutOfMemoryError
+                slots, ok = [], 0
+            flag = torch.tensor([ok], dtype=torch.int32, device=dev)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            if int(flag.item()) == 1:
+                for s in slots:
+                    h = symm_mem.rendezvous(s, dist.group.WORLD)
+                    self.peers.append([h.get_buffer(p, (self.total,), torch.uint8) for p in range(world)])
+                self.slots, self.sharded = slots, True
+        if not self.sharded:
+            self.slots = [torch.empty(self.total, dtype=torch.uint8, device=dev) for _ in range(2)]
+        self.gloo = gloo_group
+        self.bounds = byte_parts(self.total, world) if self.sharded else [0, self.total]
+        mine = (self.bounds[rank], self.bounds[rank + 1]) if self.sharded else (0, self.total)
+        self.mine = mine
+        self.views = [[s[o:o + x.nbytes].view(x.dtype).view(x.shape) for x, o in zip(inputs, self.offs)]
+                      for s in self.slots]
+        self.copy_stream = torch.cuda.Stream(dev)
+        self.compute_done = [torch.cuda.Event() for _ in range(2)]
+        self.copied = [torch.cuda.Event() for _ in range(2)]
+        for ev in self.compute_done:
+            ev.record()
+
+    @property
+    def h2d_bytes(self) -> int:
+        return self.mine[1] - self.mine[0]
+
+    @property
+    def peer_bytes(self) -> int:
+        return self.total - self.h2d_bytes if self.sharded else 0
+
+    def _produce(self, nsteps, state):
+        import torch.distributed as dist
+
+        try:
+            torch.cuda.set_device(self.dev)
+            cs = self.copy_stream
+            lo, hi = self.mine
+            for k in range(nsteps):
+                s = k % 2
+                with state["cv"]:
+                    # the main thread has enqueued step k - 2 (recorded its compute_done)
+                    if not state["cv"].wait_for(lambda: state["enqueued"] >= k - 1 or state["stop"], timeout=300):
+                        raise TimeoutError(f"loader: step {k - 2} was never enqueued")
+                    if state["stop"]:
+                        return
+                with torch.cuda.stream(cs):
+                    cs.wait_event(self.compute_done[s])
+                    if hi > lo:
+                        self.slots[s][lo:hi].copy_(self.host[lo:hi], non_blocking=True)
+                cs.synchronize()
+                if self.sharded:
+                    dist.barrier(group=self.gloo)
+                    with torch.cuda.stream(cs):
+                        for p in range(self.world):
+                            a, b = self.bounds[p], self.bounds[p + 1]
+                            if p != self.rank and b > a:
+                                self.slots[s][a:b].copy_(self.peers[s][p][a:b], non_blocking=True)
+                with torch.cuda.stream(cs):
+                    self.copied[s].record(cs)
+                cs.synchronize()
+                with state["cv"]:
+                    state["ready"] = k + 1
+                    state["cv"].notify_all()
+        except BaseException as e:  # surfaced by run()
+            with state["cv"]:
+                state["error"] = e
+                state["cv"].notify_all()
+
+    def run(self, nsteps, step, out_host):
+        """``nsteps`` steps of ``step(*inputs)``, each fed by the loader; every step's logps
+        (``out[0]``) are read back into ``out_host``."""
+        import threading
+
+        state = {"cv": threading.Condition(), "enqueued": 0, "ready": 0, "stop": False, "error": None}
+        t = threading.Thread(target=self._produce, args=(nsteps, state), daemon=True)
+        t.start()
+        try:
+            for k in range(nsteps):
+                s = k % 2
+                with state["cv"]:
+                    state["cv"].wait_for(lambda: state["ready"] > k or state["error"] is not None, timeout=600)
+                    if state["error"] is not None:
+                        raise RuntimeError("step-input loader failed") from state["error"]
+                    if state["ready"] <= k:
+                        raise TimeoutError(f"loader: inputs of step {k} never arrived")
+                torch.cuda.current_stream().wait_event(self.copied[s])
+                out = step(*self.views[s])
+                self.compute_done[s].record()
+                out_host.copy_(out[0].detach(), non_blocking=True)
+                with state["cv"]:
+                    state["enqueued"] = k + 1
+                    state["cv"].notify_all()
+        finally:
+            with state["cv"]:
+                state["stop"] = True
+                state["cv"].notify_all()
+            t.join()
+
+
 # --------------------------------------------------------------------------- CUDA arm
-def measure(args, wl, *, dev, rank, world, local, clocks):
+def measure(args, wl, *, dev, rank, world, local, clocks, gloo_group=None):
     """Warm-up, device-resident timing, end-to-end timing, parity, roofline; the JSON line."""
     import torch.distributed as dist
 
@@ -641,55 +795,39 @@ def measure(args, wl, *, dev, rank, world, local, clocks):
     # ---------------------------------------------------------------- end-to-end (host buffers)
     e2e = None
     if not args.no_e2e:
-        # Every step copies its inputs from pinned host memory and reads its logps back. The
-        # inputs are double-buffered: step k+1's host->device copies run on a copy stream
-        # (copy engines) while step k computes, as a data loader would feed the trainer.
-        hosts = [x.detach().cpu().pin_memory() for x in wl.inputs]
-        bufs = [[torch.empty_like(x) for x in wl.inputs] for _ in range(2)]
+        # Every step copies its inputs from pinned host memory and reads its logps back
+        # (StepLoader: double-buffered on the copy engines; with N ranks each rank copies 1/N
+        # of the bytes from host and pulls the rest from its peers over NVLink).
+        loader = StepLoader(wl.inputs, dev=dev, rank=rank, world=world, gloo_group=gloo_group)
         out_host = torch.empty(wl.out_shape, dtype=torch.float32).pin_memory()
-        h2d = sum(x.nbytes for x in hosts)
         d2h = out_host.nbytes
-        copy_stream = torch.cuda.Stream(dev)
-        compute_done = [torch.cuda.Event() for _ in range(2)]
-        copied = [torch.cuda.Event() for _ in range(2)]
-        for ev in compute_done:
-            ev.record()
-
-        def issue_copy(k):
-            b = k % 2
-            with torch.cuda.stream(copy_stream):
-                copy_stream.wait_event(compute_done[b])  # step k-2 no longer reads buffer b
-                for hx, dx in zip(hosts, bufs[b]):
-                    dx.copy_(hx, non_blocking=True)
-                copied[b].record(copy_stream)
-
-        def e2e_run(nsteps):
-            issue_copy(0)
-            for k in range(nsteps):
-                b = k % 2
-                if k + 1 < nsteps:
-                    issue_copy(k + 1)
-                torch.cuda.current_stream().wait_event(copied[b])
-                out = wl.step(*bufs[b])
-                compute_done[b].record()
-                out_host.copy_(out[0].detach(), non_blocking=True)
-
-        e2e_run(args.warmup)
+        loader.run(args.warmup, wl.step, out_host)
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t_wall0 = time.time()
         e0.record()
-        e2e_run(args.steps)
+        loader.run(args.steps, wl.step, out_host)
         e1.record()
         torch.cuda.synchronize()
         windows.append((t_wall0, time.time()))
         barrier()
         ems = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        # the bytes every slot holds after the run are the step inputs (own range from host,
+        # the rest from the peers), on every rank
+        same = all(torch.equal(v, x) for s in range(2) for v, x in zip(loader.views[s], wl.inputs))
+        inputs_ok = max_over_ranks(0.0 if same else 1.0) == 0.0
         e2e = {"value": wl.n_valid / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems,
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
-        del hosts, bufs
+               "h2d_bytes_per_step": int(loader.h2d_bytes), "d2h_bytes_per_step": int(d2h),
+               "h2d_bytes_per_step_all_ranks": int(loader.total if loader.sharded else loader.total * world),
+               "nvlink_bytes_per_step": int(loader.peer_bytes), "inputs_ok": bool(inputs_ok),
+               "loader": ("each rank copies 1/N of the step inputs from pinned host memory and pulls the rest "
+                          "from its peers over NVLink" if loader.sharded else
+                          "every rank copies all step inputs from pinned host memory")}
+        del loader
+        torch.cuda.synchronize()
+        barrier()
 
     # ---------------------------------------------------------------- parity of one step
     parity = None
@@ -814,7 +952,7 @@ def measure(args, wl, *, dev, rank, world, local, clocks):
             "cta_group": cta_group_of_run(),
         }
         print(json.dumps(line), flush=True)
-    return parity is None or parity["ok"]
+    return (parity is None or parity["ok"]) and (e2e is None or e2e["inputs_ok"])
 
 
 def main():
@@ -842,11 +980,14 @@ def main():
     if args.cta_group:
         _lib.set_cta_group(args.cta_group)
     mesh = None
+    gloo_group = None
     if world > 1:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
         mesh = VocabMesh(None)
+        # host-only barriers of the step-input loader (its background thread)
+        gloo_group = dist.new_group(backend="gloo", timeout=timedelta(seconds=120))
 
     softcap = args.softcap if args.softcap > 0 else None
     chunk = args.token_chunk or None
@@ -857,12 +998,13 @@ def main():
     try:
         if args.config == 2:
             ok = measure(args, grpo_workload(args, dev, rank, world, mesh, softcap, chunk), dev=dev, rank=rank,
-                         world=world, local=local, clocks=clocks)
+                         world=world, local=local, clocks=clocks, gloo_group=gloo_group)
         else:
             tokens = [int(t) for t in args.tokens.split(",") if t.strip()] or [DENSE_CONFIGS[args.config][0]]
             for T_cfg in tokens:
                 wl = dense_workload(args, dev, rank, world, mesh, softcap, chunk, T_cfg)
-                ok = measure(args, wl, dev=dev, rank=rank, world=world, local=local, clocks=clocks) and ok
+                ok = measure(args, wl, dev=dev, rank=rank, world=world, local=local, clocks=clocks,
+                             gloo_group=gloo_group) and ok
                 del wl
                 torch.cuda.empty_cache()
     finally:
