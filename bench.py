@@ -647,6 +647,8 @@ class StepLoader:
         self.views = [[s[o:o + x.nbytes].view(x.dtype).view(x.shape) for x, o in zip(inputs, self.offs)]
                       for s in self.slots]
         self.copy_stream = torch.cuda.Stream(dev)
+        # one stream per peer, so the pulls run on several copy engines at once
+        self.pull_streams = [torch.cuda.Stream(dev) for _ in range(world - 1)] if self.sharded else []
         self.compute_done = [torch.cuda.Event() for _ in range(2)]
         self.copied = [torch.cuda.Event() for _ in range(2)]
         for ev in self.compute_done:
@@ -682,11 +684,13 @@ class StepLoader:
                 cs.synchronize()
                 if self.sharded:
                     dist.barrier(group=self.gloo)
-                    with torch.cuda.stream(cs):
-                        for p in range(self.world):
-                            a, b = self.bounds[p], self.bounds[p + 1]
-                            if p != self.rank and b > a:
+                    others = [p for p in range(self.world) if p != self.rank]
+                    for p, ps in zip(others, self.pull_streams):
+                        a, b = self.bounds[p], self.bounds[p + 1]
+                        if b > a:
+                            with torch.cuda.stream(ps):
                                 self.slots[s][a:b].copy_(self.peers[s][p][a:b], non_blocking=True)
+                        cs.wait_stream(ps)
                 with torch.cuda.stream(cs):
                     self.copied[s].record(cs)
                 cs.synchronize()
