@@ -126,17 +126,20 @@ int forced_cta_group() {
   return v;
 }
 
-// CTA group per GEMM. The forward and the dZ recompute carry heavy epilogues (softcap and
-// exp per logit) and measured faster as single CTAs; the dH and dW GEMMs (plain stores)
-// measured faster as CTA pairs.
-enum CgUse { CG_FWD, CG_DZ, CG_DH, CG_DW, CG_HOOK };
+// CTA group per GEMM. A pair's 256x256 tile takes a third less operand data from L2 per FLOP
+// than two single-CTA 128x256 tiles, and at the 1 kW power cap the energy saved comes back as
+// SM clock. With one multicast commit per K block the pair's MMA issue is as fast as a single
+// CTA's (forward: 659 vs 652 cycles per K block); a whole config-2 step with every GEMM as
+// pairs measured fastest, although the dZ recompute alone is ~2 % faster as single CTAs.
+// The sampler head (a few decode rows) and the generic GEMM hook use single CTAs.
+enum CgUse { CG_FWD, CG_DZ, CG_DH, CG_DW, CG_HOOK, CG_HEAD };
 int cta_group_for(CgUse k) {
   const int f = forced_cta_group();
   if (f) return f;
   // tuning: LP_B200_CG_PER_GEMM="fzhw" (four digits 1 / 2: forward, dZ, dH, dW)
   static const char* per = getenv("LP_B200_CG_PER_GEMM");
   if (per != nullptr && k < CG_HOOK && (int)strlen(per) >= 4 && (per[k] == '1' || per[k] == '2')) return per[k] - '0';
-  return (k == CG_DH || k == CG_DW) ? 2 : 1;
+  return (k == CG_HOOK || k == CG_HEAD) ? 1 : 2;
 }
 int cta_group() { return forced_cta_group(); }
 
@@ -720,7 +723,7 @@ extern "C" {
 
 size_t lp_head_workspace_bytes(int64_t B, int64_t V) {
   if (B <= 0 || V <= 0) return 256;
-  const int cg = cta_group_for(CG_FWD);
+  const int cg = cta_group_for(CG_HEAD);
   return 2 * head_part_bytes(plan_head(B, V, 64, 128 * cg), B);
 }
 
@@ -746,7 +749,7 @@ int lp_head(void* stream, const void* H, int64_t B, int64_t d, int64_t ldh, cons
   int rc = current_device_info(&di);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int cg = cta_group_for(CG_FWD);
+  const int cg = cta_group_for(CG_HEAD);
   GemmSched s = plan_head(B, V, d, 128 * cg);
   const size_t pb = head_part_bytes(s, B);
   if (workspace == nullptr || workspace_bytes < 2 * pb)

@@ -54,6 +54,11 @@
 #ifndef LP_STAGES_CG2
 #define LP_STAGES_CG2 6
 #endif
+// 1: the pair's MMA thread signals a barrier in both CTAs with one multicast commit; 0: one
+// commit per CTA.
+#ifndef LP_PAIR_COMMIT_BOTH
+#define LP_PAIR_COMMIT_BOTH 1
+#endif
 #ifndef LP_STAGES_CG2_STORE
 #define LP_STAGES_CG2_STORE 5
 #endif
@@ -535,6 +540,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // free the smem stage (in every CTA of the pair) once these MMAs have read it
             if constexpr (CG == 1) {
               mma_commit(&empty_bar[s]);
+            } else if (LP_PAIR_COMMIT_BOTH) {
+              mma_commit_pair_both(smem_u32(&empty_bar[s]), 0x3);
             } else {
               const uint32_t eb = smem_u32(&empty_bar[s]);
               mma_commit_pair(mapa_shared(eb, 0));
@@ -545,6 +552,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // accumulator ready for the epilogue warps (of every CTA of the pair)
           if constexpr (CG == 1) {
             mma_commit(&tfull_bar[buf]);
+          } else if (LP_PAIR_COMMIT_BOTH) {
+            mma_commit_pair_both(smem_u32(&tfull_bar[buf]), 0x3);
           } else {
             const uint32_t fb = smem_u32(&tfull_bar[buf]);
             mma_commit_pair(mapa_shared(fb, 0));

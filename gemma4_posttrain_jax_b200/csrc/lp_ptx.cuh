@@ -520,4 +520,12 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
                : "memory");
 }
 
+// One commit of the pair's MMAs that arrives on the mbarrier at this CTA-local shared
+// address in every CTA of `cta_mask` (a signal to the pair's own barriers; no data moves).
+__device__ __forceinline__ void mma_commit_pair_both(uint32_t smem_addr, uint16_t cta_mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               ::"r"(smem_addr), "h"(cta_mask)
+               : "memory");
+}
+
 }  // namespace lpk
