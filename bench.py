@@ -55,14 +55,22 @@ METRIC = "logprob fwd+bwd tokens/s @V=262144,d=2048 (GRPO response tokens, vocab
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch of the forward GEMM on this workload at N=1: a stored
 # constant, not measured by this run. It comes from an ncu capture of the batch-16 case of
-# this workload (13,969 tokens: 2.638 GB read + 0.061 GB written by the forward launch of
+# this workload (13,969 tokens: 2.766 GB read + 0.061 GB written by the forward launch, CTA
+# pairs, of
 # ``ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
 # --clock-control none -k regex:tc_gemm -s 39 -c 13 python bench.py --batch 16 --steps 1
 # --warmup 3 --no-e2e --no-cpu-baseline --no-parity --token-chunk 4096``), scaled by the
 # tokens of the full batch (the forward streams W once per 12,288-token block of hidden
 # rows, so its traffic grows in proportion to the token count at a fixed vocabulary).
-NCU_FWD_TRAFFIC_PER_TOKEN_N1 = (2.638e9 + 0.061e9) / 13969
+NCU_FWD_TRAFFIC_PER_TOKEN_N1 = (2.766e9 + 0.061e9) / 13969
 NCU_TRAFFIC_NOTE = "stored constant: ncu DRAM bytes of the forward GEMM per token (batch-16 capture), x tokens"
+# The same capture's dZ GEMM launches (4096-row chunks): 1.093 GB read (W once, the chunk's
+# hidden rows) + 2.109 GB written (the chunk's bf16 dZ). A launch reads W once as long as its
+# chunk is at most one 12,288-row block, so its traffic is that read plus its rows' writes.
+NCU_DZ_READ_PER_LAUNCH_N1 = 1.093e9
+NCU_DZ_WRITE_PER_ROW_N1 = 2.109e9 / 4096
+NCU_DZ_TRAFFIC_NOTE = ("stored constant: ncu DRAM bytes of a dZ GEMM launch (batch-16 capture): W read once "
+                       "+ dZ bytes written per row x rows per launch")
 LOGP_ATOL, GRAD_RTOL = 2e-3, 1e-2
 
 # Dense-token BASELINE configs: (tokens, hidden, frozen head, extra forward-only pass).
@@ -864,9 +872,14 @@ def measure(args, wl, *, dev, rank, world, local, clocks, gloo_group=None):
         cnt = prof[dom][1]
         flop_per_launch = wl.flops[dom] * args.steps / max(cnt, 1)
         achieved = flop_per_launch / (kernels[dom]["ms_per_launch"] / 1e3) / 1e12
-        traffic = None
+        traffic, traffic_note = None, None
         if wl.traffic_ok and dom == "fwd_lse_gemm":
-            traffic = NCU_FWD_TRAFFIC_PER_TOKEN_N1 * wl.n_valid
+            traffic, traffic_note = NCU_FWD_TRAFFIC_PER_TOKEN_N1 * wl.n_valid, NCU_TRAFFIC_NOTE
+        elif wl.traffic_ok and dom == "bwd_dz_gemm":
+            rows_per_launch = wl.n_bwd * args.steps / max(cnt, 1)
+            if rows_per_launch <= 12288:
+                traffic = NCU_DZ_READ_PER_LAUNCH_N1 + NCU_DZ_WRITE_PER_ROW_N1 * rows_per_launch
+                traffic_note = NCU_DZ_TRAFFIC_NOTE
         roofline = {
             "kernel": dom,
             "bound": "tensor",
@@ -876,7 +889,7 @@ def measure(args, wl, *, dev, rank, world, local, clocks, gloo_group=None):
             "frac": achieved / peaks["bf16_tflops_sustained"],
             "traffic": traffic,
             "traffic_unit": "bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum)",
-            "traffic_source": NCU_TRAFFIC_NOTE if traffic is not None else None,
+            "traffic_source": traffic_note,
             "peak_source": f"bf16_tflops_sustained ({peak_src}); kernel runs inside a long step",
             "flop_per_launch": flop_per_launch,
         }
