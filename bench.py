@@ -912,8 +912,14 @@ def measure(args, wl, *, dev, rank, world, local, clocks, gloo_group=None):
         parts = {"fwd_exchange_ms": kms("fwd_finalize_mesh"), "peer_barrier_ms": kms("peer_barrier"),
                  "nccl_ms": nccl, "dh_sum_in_gemm_ms_est": dh_over}
         total = sum(parts.values())
+        # every rank's own figure: the rank that waits least is normally the slowest GPU,
+        # whose time sets the step; the others' waits are slack behind it
+        lo, hi = -max_over_ranks(-total), max_over_ranks(total)
         collective = {**parts, "exposed_collective_ms": total, "frac_of_step": total / ms,
-                      "note": "fwd_exchange includes the wait for the slowest rank's forward GEMM"}
+                      "exposed_collective_ms_min_over_ranks": lo, "exposed_collective_ms_max_over_ranks": hi,
+                      "frac_of_step_min_over_ranks": lo / ms,
+                      "note": "rank 0's kernel timings; fwd_exchange includes the wait for the slowest rank's "
+                              "forward GEMM; min over ranks = the least-waiting rank (normally the slowest GPU)"}
 
     # ---------------------------------------------------------------- CPU baseline (rank 0, N = 1)
     cpu = None
