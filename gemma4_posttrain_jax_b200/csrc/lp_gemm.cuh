@@ -35,8 +35,8 @@
 //
 // Synchronisation (all waits bounded, see lp_ptx.cuh):
 //   full[s]   : TMA -> MMA. CG=2: lives in the leader, counts both CTAs' bytes.
-//   empty[s]  : MMA -> TMA, in every CTA; the MMA thread commits to each CTA's copy.
-//   tfull[b]  : MMA -> epilogue, in every CTA (commit per CTA).
+//   empty[s]  : MMA -> TMA, in every CTA; CG=2: one multicast commit arrives on both copies.
+//   tfull[b]  : MMA -> epilogue, in every CTA (CG=2: one multicast commit).
 //   tempty[b] : epilogue -> MMA, in the leader; every epilogue warp of the pair arrives.
 #pragma once
 

@@ -68,8 +68,9 @@ LP_API const char* lp_last_error(void);
 LP_API long long lp_launch_count(void);
 
 /* Tensor-core CTA group of the GEMMs: 0 (default) lets each GEMM use the group measured
- * faster for it (single CTAs, 128x256 tiles, for the forward and the dZ recompute; CTA pairs
- * on two SMs, 256x256 tiles, for dH and dW); 1 or 2 forces one group for every GEMM (also
+ * faster for it (CTA pairs on two SMs, 256x256 tiles, for the forward, the dZ recompute, dH
+ * and dW; single CTAs, 128x256 tiles, for the sampler head and for the dW GEMM of a token
+ * chunk of at most 1024 rows); 1 or 2 forces one group for every GEMM (also
  * LP_B200_CTA_GROUP=1|2). Results agree to f32 rounding; lp_get_cta_group() returns the
  * forced group or 0. */
 LP_API int lp_set_cta_group(int cg);
