@@ -46,8 +46,10 @@
 // staging (single CTAs: 4 x 48 KB; pairs: 6 x 32 KB, or 5 x 32 KB beside the 64 KB of
 // 128-byte store staging of the plain-store GEMMs). Measured (pipeline counters, config-2
 // workload): the single-CTA forward waits 639 / 207 / 103 cycles per K block for its loads
-// with 2 / 3 / 4 stages; the pairs gain nothing from a 6th stage over 5. Overridable at
-// build time for tuning.
+// with 2 / 3 / 4 stages; the pairs gain nothing from a 6th stage over 5, and the pair forward
+// (no staging, so 7 x 32 KB fit) waits 146 instead of 94 cycles per K block with a 7th and
+// runs 6 % slower: more loads in flight only queue longer. Overridable at build time for
+// tuning.
 #ifndef LP_STAGES_CG1
 #define LP_STAGES_CG1 4
 #endif
@@ -61,6 +63,9 @@
 #endif
 #ifndef LP_STAGES_CG2_STORE
 #define LP_STAGES_CG2_STORE 5
+#endif
+#ifndef LP_STAGES_CG2_FWD
+#define LP_STAGES_CG2_FWD LP_STAGES_CG2
 #endif
 
 namespace lpk {
@@ -101,7 +106,8 @@ __host__ __device__ constexpr int staging_buf_bytes() {
 
 template <int CG, int EPI>
 __host__ __device__ constexpr int num_stages() {
-  return CG == 1 ? LP_STAGES_CG1 : (EPI == EPI_STORE ? LP_STAGES_CG2_STORE : LP_STAGES_CG2);
+  return CG == 1 ? LP_STAGES_CG1
+                 : (EPI == EPI_STORE ? LP_STAGES_CG2_STORE : (EPI == EPI_FWD_LSE ? LP_STAGES_CG2_FWD : LP_STAGES_CG2));
 }
 
 struct GemmSched {
