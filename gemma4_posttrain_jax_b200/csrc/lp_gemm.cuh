@@ -46,10 +46,11 @@
 // staging (single CTAs: 4 x 48 KB; pairs: 6 x 32 KB, or 5 x 32 KB beside the 64 KB of
 // 128-byte store staging of the plain-store GEMMs). Measured (pipeline counters, config-2
 // workload): the single-CTA forward waits 639 / 207 / 103 cycles per K block for its loads
-// with 2 / 3 / 4 stages; the pairs gain nothing from a 6th stage over 5, and the pair forward
-// (no staging, so 7 x 32 KB fit) waits 146 instead of 94 cycles per K block with a 7th and
-// runs 6 % slower: more loads in flight only queue longer. Overridable at build time for
-// tuning.
+// with 2 / 3 / 4 stages. Pairs, per K block: the forward waits 98 / 94 / 146 cycles with
+// 5 / 6 / 7 stages (7 x 32 KB fit without store staging; with 7 it runs 6 % slower: more
+// loads in flight only queue longer), the dZ GEMM 140 / 122 with 5 / 6, dH and dW 125 / 88 and
+// 169 / 124 with 4 / 5: the defaults are the best depth each way. Overridable at build time
+// for tuning.
 #ifndef LP_STAGES_CG1
 #define LP_STAGES_CG1 4
 #endif
